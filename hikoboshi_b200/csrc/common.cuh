@@ -1,0 +1,114 @@
+// Shared device-side definitions for the ProteinMPNN v_48_020 design engine.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace hkb {
+
+constexpr int kH = 128;         // hidden width
+constexpr int kK = 48;          // neighbours per residue (max)
+constexpr int kV = 21;          // vocabulary "ACDEFGHIKLMNPQRSTVWYX"
+constexpr int kFfn = 512;       // FFN hidden
+constexpr int kEdgeIn = 416;    // 16 positional + 25 pairs x 16 RBF
+constexpr int kRbf = 16;
+constexpr int kPairs = 25;
+constexpr int kPosClasses = 66;
+constexpr float kMessageScale = 30.0f;
+constexpr float kLnEps = 1.0e-5f;
+
+// Device error word bits (read by the host after each call; kernels never
+// trap, they record and return).
+enum DeviceError : unsigned int {
+  kErrNone = 0,
+  kErrBadIndex = 1u << 0,
+  kErrTimeout = 1u << 1,
+  kErrTmemAlloc = 1u << 2,
+};
+
+// exp(x) for x <= 0: integer range reduction against e^-n (n = 0..16) and a
+// 6th-order Taylor polynomial for the remainder r in [-0.5, 0.5]; 0 below -16
+// (the reference's rule, cpp/include/hikoboshi/primitives/detail/
+// fast_exp_neg.hpp:9-52).  The table holds e^-n rounded to float.
+static __constant__ float c_exp_neg_table[17] = {
+    1.0f, 0.3678794503211975f, 0.1353352814912796f, 0.049787066876888275f,
+    0.018315639346837997f, 0.0067379469983279705f, 0.0024787522852420807f,
+    0.0009118819725699723f, 0.000335462624207139f, 0.00012340980174485594f,
+    4.539993096841499e-05f, 1.6701700587873347e-05f, 6.1442124206223525e-06f,
+    2.260329438286135e-06f, 8.315287232107949e-07f, 3.0590231858695915e-07f,
+    1.1253517584464134e-07f};
+
+__device__ __forceinline__ float exp_neg(float x) {
+  if (x != x) return x;
+  float nx = -x;
+  if (nx > 16.0f) return 0.0f;
+  if (nx < 0.0f) nx = 0.0f;
+  int n = __float2int_rz(__fadd_rn(nx, 0.5f));
+  if (n > 16) n = 16;
+  const float r = -__fsub_rn(nx, (float)n);
+  float p = __fadd_rn(1.0f / 120.0f, __fmul_rn(r, 1.0f / 720.0f));
+  p = __fadd_rn(1.0f / 24.0f, __fmul_rn(r, p));
+  p = __fadd_rn(1.0f / 6.0f, __fmul_rn(r, p));
+  p = __fadd_rn(0.5f, __fmul_rn(r, p));
+  p = __fadd_rn(1.0f, __fmul_rn(r, p));
+  p = __fadd_rn(1.0f, __fmul_rn(r, p));
+  return __fmul_rn(c_exp_neg_table[n], p);
+}
+
+// GELU(x) = x/2 (1 + erf(x / sqrt 2)), erf by Abramowitz & Stegun 7.1.26
+// with exp(-v^2) from exp_neg (reference: cpp/include/hikoboshi/primitives/
+// compute/gelu.hpp:22-51).  Used by the fp32 parity path.
+__device__ __forceinline__ float gelu_as(float x) {
+  float v = x * 0.7071067811865475f;
+  float sign = 1.0f;
+  if (v < 0.0f) {
+    sign = -1.0f;
+    v = -v;
+  }
+  float e;
+  if (v > 4.0f) {
+    e = sign;
+  } else {
+    const float t = __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(0.3275911f, v)));
+    float p = 1.061405429f * t + -1.453152027f;
+    p = p * t + 1.421413741f;
+    p = p * t + -0.284496736f;
+    p = p * t + 0.254829592f;
+    p = p * t;
+    e = sign * (1.0f - p * exp_neg(-(v * v)));
+  }
+  return 0.5f * x * (1.0f + e);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// LayerNorm of a 128-wide row held 4 values per lane by one warp:
+// two-pass mean / population variance, eps 1e-5 (reference semantics:
+// cpp/primitives/compute/layer_norm_scalar.cpp:8-40 computes the same
+// statistics with Welford's update).
+__device__ __forceinline__ void warp_layer_norm128(float (&x)[4], const float* g,
+                                                  const float* b, int lane) {
+  float s = warp_sum(x[0] + x[1] + x[2] + x[3]);
+  const float mean = s * (1.0f / 128.0f);
+  float d0 = x[0] - mean, d1 = x[1] - mean, d2 = x[2] - mean, d3 = x[3] - mean;
+  float v = warp_sum(d0 * d0 + d1 * d1 + d2 * d2 + d3 * d3) * (1.0f / 128.0f);
+  const float inv = 1.0f / sqrtf(v + kLnEps);
+  const int c = lane * 4;
+  x[0] = d0 * inv * g[c + 0] + b[c + 0];
+  x[1] = d1 * inv * g[c + 1] + b[c + 1];
+  x[2] = d2 * inv * g[c + 2] + b[c + 2];
+  x[3] = d3 * inv * g[c + 3] + b[c + 3];
+}
+
+}  // namespace hkb

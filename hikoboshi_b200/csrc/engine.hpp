@@ -1,0 +1,85 @@
+// Engine internals shared by the C ABI (engine.cu) and the bf16 path.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "hkb_mpnn.h"
+#include "kernels.hpp"
+
+namespace hkb {
+
+// Named, grow-only device buffers reused across calls.
+class Workspace {
+ public:
+  ~Workspace() { release(); }
+  void* get(const std::string& name, size_t bytes);
+  template <typename T>
+  T* get_as(const std::string& name, size_t count) {
+    return static_cast<T*>(get(name, count * sizeof(T)));
+  }
+  void release();
+  size_t bytes() const;
+
+ private:
+  struct Buf {
+    void* p = nullptr;
+    size_t n = 0;
+  };
+  std::map<std::string, Buf> bufs_;
+};
+
+// Host-side description of one validated batch.
+struct HostBatch {
+  int B = 0;
+  int R = 0;
+  int64_t Q = 0;
+  int NS = 0;
+  int max_len = 0;
+  std::vector<int> L, off, S, seq_base;
+  std::vector<int64_t> qoff;          // [B] first row of protein b
+  std::vector<int> res_prot;          // [R]
+  std::vector<int> seq_prot;          // [NS]
+  std::vector<int64_t> seq_row_off;   // [NS]
+  std::vector<uint64_t> seq_seed;     // [NS]
+  std::vector<float> seq_temp;        // [NS]
+  std::vector<float> mask;            // [R]
+  std::vector<int32_t> orders;        // [Q]
+};
+
+// Device copies of the per-batch tables + BatchView pointing at them.
+struct DeviceBatch {
+  BatchView bv;
+  const float* coords = nullptr;
+  const uint8_t* sources = nullptr;
+};
+
+struct EncoderOut {
+  int* e_idx = nullptr;   // [R,48]
+  float* d2 = nullptr;    // [R,48]
+  float* mask = nullptr;  // [R]
+  float* h_e = nullptr;   // [R,48,128]
+  float* h_v = nullptr;   // [R,128]
+};
+
+}  // namespace hkb
+
+struct hkb_engine {
+  int device = 0;
+  int precision = HKB_PRECISION_FP32;
+  cudaStream_t stream = nullptr;
+  void* d_weights = nullptr;
+  size_t weights_bytes = 0;
+  hkb::F32Weights w32{};
+  hkb::Workspace ws;
+  unsigned int* d_err = nullptr;
+  void* pinned = nullptr;
+  size_t pinned_bytes = 0;
+  int64_t launches = 0;
+  float timings[4] = {0, 0, 0, 0};
+  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+};

@@ -1,0 +1,161 @@
+// Kernel launchers (host-callable) of the design engine.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace hkb {
+
+// Per-call device tables describing a batch.
+struct BatchView {
+  int num_proteins = 0;
+  int total_residues = 0;        // R
+  int64_t total_rows = 0;        // Q = sum S_b L_b
+  int num_sequences = 0;         // sum S_b
+  const int* prot_res_off = nullptr;   // [B] first residue of protein b
+  const int* prot_len = nullptr;       // [B]
+  const int* res_prot = nullptr;       // [R] protein of residue
+  const int* seq_prot = nullptr;       // [NS]
+  const int64_t* seq_row_off = nullptr;  // [NS] first row of sequence in [Q]
+};
+
+// fp32 weights in the layouts the SIMT kernels read ("T" = [in][out]).
+struct F32Weights {
+  const float* pos_w;   // [16,66]
+  const float* pos_b;   // [16]
+  const float* edge_wT; // [416,128]
+  const float* norm_e_w;
+  const float* norm_e_b;
+  const float* We_T;    // [128,128]
+  const float* We_b;
+  struct Enc {
+    const float* W1acT;   // [128,256]  [W1a | W1c] for h_i and h_j terms
+    const float* b1ac;    // [256]      [b1 | 0]
+    const float* W1bT;    // [128,128]  h_E term
+    const float* W2T; const float* b2;
+    const float* W3T; const float* b3;
+    const float* W11acT; const float* b11ac;
+    const float* W11bT;
+    const float* W12T; const float* b12;
+    const float* W13T; const float* b13;
+    const float* n1w; const float* n1b;
+    const float* n2w; const float* n2b;
+    const float* n3w; const float* n3b;
+    const float* WinT;  const float* bin;   // [128,512]
+    const float* WoutT; const float* bout;  // [512,128]
+  } enc[3];
+  struct Dec {
+    const float* W1adT;   // [128,256]  [W1a | W1d]
+    const float* b1ad;    // [256]      [b1 | 0]
+    const float* W1aT;    // [128,128]  (view into W1adT rows is strided; kept separately)
+    const float* b1;      // [128]
+    const float* W1dT;    // [128,128]
+    const float* W1bT;    // [128,128]
+    const float* Stab;    // [21,128]  W1c . W_s[v]
+    const float* W2T; const float* b2;
+    const float* W3T; const float* b3;
+    const float* n1w; const float* n1b;
+    const float* n2w; const float* n2b;
+    const float* WinT;  const float* bin;
+    const float* WoutT; const float* bout;
+  } dec[3];
+  const float* headT;   // [128,21]
+  const float* head_b;  // [21]
+};
+
+// Per-protein decoder tables produced by the decoder preparation.
+struct DecoderTables {
+  const float* PE[3];     // [R*48,128] W1b_l . h_E (no bias)
+  const float* PVenc[3];  // [R,128]    W1d_l . h_enc
+  const float* Aenc0;     // [R,128]    W1a_0 . h_enc + b1_0
+};
+
+
+// Generic fp32 GEMM: C[M,N] = act(A[M,K] . B[K,N] + bias[N]); act 0 none, 1 GELU.
+void gemm_f32(cudaStream_t st, int64_t M, int N, int K, const float* A, int lda,
+              const float* B, int ldb, const float* bias, int act, float* C,
+              int ldc);
+
+// Largest protein one call accepts (kNN keeps one 8-byte key per candidate
+// in shared memory and ranks every candidate against every other).
+constexpr int kMaxResidues = 4096;
+
+void launch_knn(cudaStream_t st, const BatchView& bv, const float* coords,
+                const uint8_t* sources, int* e_idx, float* d2, float* mask,
+                unsigned int* err, int max_len);
+
+void launch_edge_features(cudaStream_t st, const BatchView& bv,
+                          const F32Weights& w, const float* coords,
+                          const uint8_t* sources, const int* e_idx, float* feat);
+
+// out = LN(x + y (+ bias)) (* mask[row] if mask != null); rows of 128.
+void launch_ln_rows(cudaStream_t st, int64_t rows, const float* x,
+                    const float* y, const float* ybias, const float* g,
+                    const float* b, const float* row_mask,
+                    const int* row_to_mask, float* out);
+
+// Encoder pieces.
+void launch_enc_msg_in(cudaStream_t st, const BatchView& bv, const float* NAC,
+                       const float* EB, const int* e_idx, float* G1);
+void launch_enc_aggregate(cudaStream_t st, const BatchView& bv, const float* G2,
+                          const int* e_idx, const float* mask, float* S,
+                          float* cnt);
+void launch_enc_node_update(cudaStream_t st, const BatchView& bv,
+                            const float* T3, const float* cnt, const float* b3,
+                            const float* h, const float* g, const float* b,
+                            float* out);
+void launch_edge_ln_update(cudaStream_t st, const BatchView& bv, const float* U3,
+                           const int* e_idx, const float* g, const float* b,
+                           float* h_e);
+void launch_gather_rows(cudaStream_t st, int64_t rows, const int* row_res,
+                        const float* src, float* dst);
+
+// Teacher-forced pieces (rows = (sequence, residue) pairs of one chunk).
+struct TfRows {
+  int64_t rows = 0;
+  const int* row_res = nullptr;       // [rows] global residue index
+  const int64_t* row_seqbase = nullptr;  // [rows] row index of residue 0 of its sequence (chunk-local)
+  const int* row_prot = nullptr;      // [rows]
+  const int* pos = nullptr;           // [rows] position of the row's residue in its order
+  const int* tokens = nullptr;        // [rows]
+};
+void launch_tf_slot_in(cudaStream_t st, const BatchView& bv, const TfRows& tr,
+                       int layer, const float* AP, const DecoderTables& dt,
+                       const float* Stab, const int* e_idx, float* G1);
+void launch_row_slot_sum(cudaStream_t st, const BatchView& bv, const TfRows& tr,
+                         const float* G2, float* S, float* kcount);
+void launch_dec_node_update(cudaStream_t st, int64_t rows, const float* T3,
+                            const float* kcount, const float* b3,
+                            const float* h, const float* g, const float* b,
+                            float* out);
+void launch_log_softmax_rows(cudaStream_t st, int64_t rows, const float* logits,
+                             float* out);
+
+// Autoregressive decode (fused persistent kernel, fp32 SIMT).
+struct ArArgs {
+  const int* group_seq0;     // [groups] first global sequence of the group
+  const int* group_count;    // [groups]
+  int num_groups;
+  const int* orders;         // [Q]
+  int* pos;                  // [Q] scratch
+  int* tokens;               // [Q] out
+  float* log_probs;          // [Q,21] out
+  float* scores;             // [NS] out
+  float* PV;                 // [2,Q,128] scratch (zeroed by the caller)
+  const uint64_t* seq_seed;  // [NS]
+  const float* seq_temp;     // [NS]
+  const float* mask;         // [R]
+  const int* e_idx;          // [R,48]
+  const float* h_enc;        // [R,128]
+  int64_t total_rows;
+};
+void launch_ar_decode_f32(cudaStream_t st, const BatchView& bv,
+                          const F32Weights& w, const DecoderTables& dt,
+                          const ArArgs& a, unsigned int* err);
+
+int ar_f32_group_size();
+
+void launch_scores(cudaStream_t st, const BatchView& bv, const int* tokens,
+                   const float* log_probs, const float* mask, float* scores);
+
+}  // namespace hkb
