@@ -1,0 +1,385 @@
+#!/usr/bin/env python3
+"""Benchmark: ProteinMPNN v_48_020 designed residues/s.
+
+One step = one batched design over 64 synthetic backbones (generator seeds
+rank*64 + 0..63) x L=256 x 32 sequences at T=0.1 with a random decoding order
+per sequence: featurisation, encoder, decoder tables and the autoregressive
+decode of all 2,048 sequences (524,288 designed residues per GPU).
+
+* ``value``  -- inputs resident in HBM (hkb_mpnn_design_device); per-step
+  device time from CUDA events on the launching stream (host-side order
+  generation inside the interval); L2 flushed (512 MiB write) before each step.
+* ``e2e``    -- the host API (hkb_mpnn_design): pinned coords/atom-sources
+  uploaded and tokens + log-probs + scores read back every step; wall clock.
+* ``roofline`` -- the autoregressive decode kernel (the dominant kernel):
+  algorithmic FLOPs per launch (29,103,360 per designed residue, the reference
+  formulation) over its CUDA-event duration, against MEASURED_PEAKS.json.
+* ``cpu_baseline`` -- the reference's own CPU design path (oracle/_ref, the
+  reference sources compiled here) on the host cores, bounded sample.
+
+``--impl reference`` times that reference CPU path alone on the same metric.
+Multi-GPU: one process per GPU (torchrun), proteins sharded by rank, no
+collective on the data path (weak scaling); barrier + max-over-ranks timing.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L_RES = 256
+N_PROT = 64
+N_SEQ = 32
+TEMP = 0.1
+FLOP_DECODE_PER_RES = 29_103_360
+FLOP_ENCODE_PER_RES = 54_657_024
+WEIGHTS = ROOT / "hikoboshi_b200" / "weights" / "Hikoboshi-ProteinMPNN-v48-020.safetensors"
+METRIC = "ProteinMPNN v48 designed residues/sec at L=256 x32 seqs; us per decode step"
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def make_inputs(rank: int):
+    from hikoboshi_b200 import synthetic_backbone
+    cs, ss = [], []
+    for i in range(N_PROT):
+        c, s = synthetic_backbone(rank * N_PROT + i, L_RES)
+        cs.append(c)
+        ss.append(s)
+    return np.concatenate(cs), np.concatenate(ss)
+
+
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        load = [x for x, p in zip(sm, power) if p > 200] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def profiled_traffic(precision: str):
+    """dram read+write bytes per launch of the decode kernel, from the
+    committed ncu summary of the same workload (None if not captured)."""
+    f = ROOT / "profiles" / f"ar_decode_{precision}_config2.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+def cpu_baseline_sample(threads: int, seqs_per_thread: int = 1):
+    """The reference's design path (algorithms::inverse_fold_proteinmpnn_v48_020
+    compiled from its sources) on `threads` host threads, each designing
+    `seqs_per_thread` sequences of its own config-2 backbone (L=256, T=0.1,
+    random order).  Returns (residues/s, description)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from hikoboshi_b200 import synthetic_backbone
+    from oracle.oracle import RefLib
+
+    ref = RefLib(WEIGHTS)
+    inputs = [synthetic_backbone(i % N_PROT, L_RES) for i in range(threads)]
+
+    def one(i):
+        c, s = inputs[i]
+        ref.design(c, s, seqs_per_thread, seed=1000 + i, temperature=TEMP, decode_order=0,
+                   keep_log_probs=True)
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(one, range(threads)))
+    dt = time.perf_counter() - t0
+    res = threads * seqs_per_thread * L_RES
+    desc = (f"{threads} threads x {seqs_per_thread} seq of L=256 (config-2 backbones, T=0.1, "
+            f"random order) through the reference design path: {res} residues in {dt:.2f} s")
+    return res / dt, desc
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    cores = host_cores()
+    for _ in range(args.warmup):
+        cpu_baseline_sample(cores)
+    vals = []
+    t0 = time.perf_counter()
+    desc = ""
+    for _ in range(args.steps):
+        v, desc = cpu_baseline_sample(cores)
+        vals.append(v)
+    wall = time.perf_counter() - t0
+    value = float(np.mean(vals))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "residues/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": wall * 1000 / max(1, args.steps), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2 sample: bounded per-step sample of 64 x L256 x 32 "
+                               "seqs design, T=0.1, random order",
+                   "proteins": N_PROT, "residue_count": L_RES, "seqs_per_protein": N_SEQ},
+        "cpu_baseline": {"value": value, "unit": "residues/s", "cores": cores,
+                         "kind": "reference", "sample": desc},
+        "e2e": {"value": value, "unit": "residues/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    from hikoboshi_b200 import DesignEngine
+    from hikoboshi_b200 import _lib as hl
+
+    eng = DesignEngine(WEIGHTS, device=local, precision=args.precision)
+    coords_h, src_h = make_inputs(rank)
+    R = coords_h.shape[0]
+    Q = N_PROT * N_SEQ * L_RES
+    NS = N_PROT * N_SEQ
+    L = np.full(N_PROT, L_RES, np.int32)
+    S = np.full(N_PROT, N_SEQ, np.int32)
+    seeds = (np.arange(N_PROT, dtype=np.uint64) + np.uint64(rank * N_PROT)) * np.uint64(1000)
+    temps = np.full(N_PROT, TEMP, np.float32)
+    modes = np.zeros(N_PROT, np.int32)
+    P = ctypes.POINTER
+
+    def batch(cp, sp):
+        return hl.DesignBatch(N_PROT, L.ctypes.data_as(P(ctypes.c_int32)), cp, sp,
+                              S.ctypes.data_as(P(ctypes.c_int32)),
+                              seeds.ctypes.data_as(P(ctypes.c_uint64)),
+                              temps.ctypes.data_as(P(ctypes.c_float)),
+                              modes.ctypes.data_as(P(ctypes.c_int32)), None)
+
+    # device-resident inputs and outputs
+    d_coords = torch.from_numpy(coords_h).to(dev)
+    d_src = torch.from_numpy(src_h).to(dev)
+    d_tok = torch.empty(Q, dtype=torch.int32, device=dev)
+    d_lp = torch.empty(Q * 21, dtype=torch.float32, device=dev)
+    d_ord = torch.empty(Q, dtype=torch.int32, device=dev)
+    d_sc = torch.empty(NS, dtype=torch.float32, device=dev)
+    bdev = batch(ctypes.c_void_p(d_coords.data_ptr()), ctypes.c_void_p(d_src.data_ptr()))
+    odev = hl.DesignOut(ctypes.c_void_p(d_tok.data_ptr()), ctypes.c_void_p(d_lp.data_ptr()),
+                        ctypes.c_void_p(d_ord.data_ptr()), ctypes.c_void_p(d_sc.data_ptr()))
+    # A dedicated stream: the engine launches on it, the events time it.
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    flush = torch.empty(128 * 1024 * 1024, dtype=torch.float32, device=dev)  # 512 MiB
+
+    def device_step():
+        st = hl.load().hkb_mpnn_design_device(eng._h, ctypes.byref(bdev), ctypes.byref(odev),
+                                              ctypes.c_void_p(stream.cuda_stream))
+        hl.check(st)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(3, args.warmup)):
+        flush.zero_()
+        device_step()
+    barrier()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    step_ms, decode_ms, launches = [], [], 0
+    t_wall0 = time.perf_counter()
+    for _ in range(args.steps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        device_step()
+        e1.record(stream)
+        e1.synchronize()
+        step_ms.append(e0.elapsed_time(e1))
+        decode_ms.append(eng.last_timings()["decode_ms"])
+        launches += eng.last_launch_count()
+    barrier()
+    wall_s = time.perf_counter() - t_wall0
+    clk = clocks.stop()
+
+    # end-to-end through the host API, pinned host buffers
+    pin_c = torch.from_numpy(coords_h).pin_memory()
+    pin_s = torch.from_numpy(src_h).pin_memory()
+    h_tok = torch.empty(Q, dtype=torch.int32).pin_memory()
+    h_lp = torch.empty(Q * 21, dtype=torch.float32).pin_memory()
+    h_sc = torch.empty(NS, dtype=torch.float32).pin_memory()
+    bh = batch(ctypes.c_void_p(pin_c.data_ptr()), ctypes.c_void_p(pin_s.data_ptr()))
+    oh = hl.DesignOut(ctypes.c_void_p(h_tok.data_ptr()), ctypes.c_void_p(h_lp.data_ptr()),
+                      None, ctypes.c_void_p(h_sc.data_ptr()))
+
+    def host_step():
+        hl.check(hl.load().hkb_mpnn_design(eng._h, ctypes.byref(bh), ctypes.byref(oh)))
+
+    host_step()
+    barrier()
+    e2e_steps = max(1, min(args.steps, 5))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        host_step()
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    barrier()
+
+    step_s = float(np.mean(step_ms)) / 1000.0
+    dec_s = float(np.mean(decode_ms)) / 1000.0
+    stats = torch.tensor([step_s, dec_s, e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    step_s, dec_s, e2e_s = stats.tolist()
+
+    if rank == 0:
+        res_step = Q * world
+        value = res_step / step_s
+        peaks, kind = measured_peaks()
+        peak = peaks["bf16_tflops_sustained"] if args.precision == "bf16" else peaks["bf16_tflops"]
+        achieved = FLOP_DECODE_PER_RES * Q / dec_s / 1e12
+        traffic = profiled_traffic(args.precision)
+        line = {
+            "metric": METRIC, "value": value, "unit": "residues/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": step_s * 1000,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if args.precision == "bf16" else "f32",
+            "data": "synthetic (seeded ideal-geometry backbones, BASELINE generator)",
+            "config": {"workload": "config2: 64 backbones x L=256 x 32 seqs per GPU, T=0.1, "
+                                   "random decoding order per sequence",
+                       "proteins_per_gpu": N_PROT, "residue_count": L_RES,
+                       "seqs_per_protein": N_SEQ, "temperature": TEMP,
+                       "precision": args.precision,
+                       "l2": "flushed before every step (512 MiB write, outside the events)"},
+            "us_per_decode_step": dec_s / L_RES * 1e6,
+            "decode_ms": dec_s * 1000,
+            "roofline": {"bound": "tensor", "kernel": "ar_decode",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "flops_per_launch": FLOP_DECODE_PER_RES * Q,
+                         "peak_kind": f"{kind} bf16 dense "
+                                      f"{'sustained' if args.precision == 'bf16' else 'burst'}"},
+            "e2e": {"value": res_step / e2e_s, "unit": "residues/s",
+                    "h2d_bytes_per_step": int(coords_h.nbytes + src_h.nbytes),
+                    "d2h_bytes_per_step": int(Q * 4 + Q * 21 * 4 + NS * 4)},
+            "gpu_launches": int(launches / max(1, args.steps)),
+            "gpu_launches_total": int(launches),
+            "clocks": clk,
+            "wall_s": wall_s,
+        }
+        if not args.no_cpu_baseline:
+            cores = host_cores()
+            v, desc = cpu_baseline_sample(cores)
+            line["cpu_baseline"] = {"value": v, "unit": "residues/s", "cores": cores,
+                                    "kind": "reference", "sample": desc}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--precision", choices=["bf16", "fp32"], default="fp32")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1088,7 +1088,18 @@ int64_t hkb_mpnn_last_launch_count(const hkb_engine* e) { return e ? e->launches
 
 hkb_status hkb_mpnn_last_timings(const hkb_engine* e, float* ms4) {
   if (e == nullptr || ms4 == nullptr) return invalid("engine and output must be non-null");
-  for (int i = 0; i < 4; ++i) ms4[i] = e->timings[i];
+  // Phases are bracketed by events on the launching stream; read them once
+  // the call's work has completed.
+  const int pairs[4][2] = {{0, 1}, {1, 2}, {2, 3}, {0, 3}};
+  for (int i = 0; i < 4; ++i) {
+    float ms = 0.0f;
+    const cudaError_t ce = cudaEventElapsedTime(&ms, e->ev[pairs[i][0]], e->ev[pairs[i][1]]);
+    if (ce != cudaSuccess) {
+      cudaGetLastError();
+      return {HKB_FAILED_PRECONDITION, cudaGetErrorString(ce)};
+    }
+    ms4[i] = ms;
+  }
   return kOk;
 }
 
