@@ -29,7 +29,7 @@ DECODE_INPUT = 2
 
 # Every symbol include/hkb_mpnn.h declares.
 EXPORTED = ["hkb_mpnn_create", "hkb_mpnn_destroy", "hkb_mpnn_design",
-            "hkb_mpnn_design_device", "hkb_mpnn_score", "hkb_mpnn_encode",
+            "hkb_mpnn_design_device", "hkb_mpnn_design_noalloc", "hkb_mpnn_score", "hkb_mpnn_encode",
             "hkb_mpnn_knn", "hkb_mpnn_decode_order", "hkb_synthetic_backbone",
             "hkb_mpnn_last_launch_count", "hkb_mpnn_last_timings",
             "hkb_mpnn_abi_version"]
@@ -91,6 +91,9 @@ def load() -> ctypes.CDLL:
     lib.hkb_mpnn_design_device.restype = Status
     lib.hkb_mpnn_design_device.argtypes = [c_void_p, POINTER(DesignBatch), POINTER(DesignOut),
                                            c_void_p]
+    lib.hkb_mpnn_design_noalloc.restype = Status
+    lib.hkb_mpnn_design_noalloc.argtypes = [c_void_p, POINTER(DesignBatch), POINTER(DesignOut),
+                                            c_void_p]
     lib.hkb_mpnn_score.restype = Status
     lib.hkb_mpnn_score.argtypes = [c_void_p, POINTER(ScoreBatch), POINTER(ScoreOut)]
     lib.hkb_mpnn_encode.restype = Status

@@ -155,6 +155,29 @@ hkb_status hkb_mpnn_knn(hkb_engine* engine, int32_t residue_count,
                         const float* coords, const uint8_t* atom_sources,
                         int32_t* e_idx, float* d2);
 
+/* Allocation-free design for small batches.  No counterpart in the
+ * reference: it exists for callers that must not allocate device memory
+ * while they run -- e.g. a plugin whose host application owns all GPU memory
+ * through its own pool allocator, or a latency-bound loop that cannot take
+ * cudaMalloc's implicit device synchronisation.  Same inputs and outputs as
+ * hkb_mpnn_design_device (device coords / atom_sources, device tokens,
+ * log_probs, orders and scores, all four required) and the same results as
+ * that entry point on an fp32 engine, for batches of at most
+ * HKB_NOALLOC_MAX_RESIDUES residues, HKB_NOALLOC_MAX_SEQUENCES sequences and
+ * HKB_NOALLOC_MAX_ROWS designed residues (larger batches: InvalidArgument).
+ * It calls no cudaMalloc / cudaFree: its scratch is one fixed device array of
+ * about 18 MiB that every GPU loading this library holds until exit.  The
+ * first call on a device looks that array's address up (one-time set-up) and
+ * should come before any stream capture.  All calls share the array, so calls
+ * whose GPU work overlaps race; the call returns after its work completes.
+ * Always runs the fp32 pipeline. */
+#define HKB_NOALLOC_MAX_RESIDUES 64
+#define HKB_NOALLOC_MAX_SEQUENCES 64
+#define HKB_NOALLOC_MAX_ROWS 1024
+hkb_status hkb_mpnn_design_noalloc(hkb_engine* engine,
+                                   const hkb_design_batch* batch,
+                                   hkb_design_out* device_out, void* stream);
+
 /* Host-only helpers (no device work) ----------------------------------- */
 
 /* Decoding order, as proteinmpnn_decode_order_scalar
