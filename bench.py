@@ -322,14 +322,14 @@ def run_ours(args):
         res_step = Q * world
         value = res_step / step_s
         peaks, kind = measured_peaks()
-        peak = peaks["bf16_tflops_sustained"] if args.precision == "bf16" else peaks["bf16_tflops"]
+        peak = peaks["bf16_tflops_sustained"] if args.precision != "fp32" else peaks["bf16_tflops"]
         achieved = FLOP_DECODE_PER_RES * Q / dec_s / 1e12
         traffic = profiled_traffic(args.precision)
         line = {
             "metric": METRIC, "value": value, "unit": "residues/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": step_s * 1000,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16" if args.precision == "bf16" else "f32",
+            "dtype": {"f16": "f16", "bf16": "bf16", "fp32": "f32"}[args.precision],
             "data": "synthetic (seeded ideal-geometry backbones, BASELINE generator)",
             "config": {"workload": "config2: 64 backbones x L=256 x 32 seqs per GPU, T=0.1, "
                                    "random decoding order per sequence",
@@ -343,8 +343,8 @@ def run_ours(args):
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "flops_per_launch": FLOP_DECODE_PER_RES * Q,
-                         "peak_kind": f"{kind} bf16 dense "
-                                      f"{'sustained' if args.precision == 'bf16' else 'burst'}"},
+                         "peak_kind": f"{kind} dense 16-bit tensor "
+                                      f"{'sustained' if args.precision != 'fp32' else 'burst'}"},
             "e2e": {"value": res_step / e2e_s, "unit": "residues/s",
                     "h2d_bytes_per_step": int(coords_h.nbytes + src_h.nbytes),
                     "d2h_bytes_per_step": int(Q * 4 + Q * 21 * 4 + NS * 4)},
@@ -373,7 +373,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--precision", choices=["bf16", "fp32"], default="fp32")
+    ap.add_argument("--precision", choices=["f16", "bf16", "fp32"], default="f16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":

@@ -23,6 +23,7 @@ STATUS_NAMES = {0: "Ok", 1: "InvalidArgument", 2: "FailedPrecondition", 3: "Unav
 
 PRECISION_FP32 = 0
 PRECISION_BF16 = 1
+PRECISION_F16 = 2
 DECODE_RANDOM = 0
 DECODE_N_TO_C = 1
 DECODE_INPUT = 2

@@ -6,6 +6,7 @@
 #include "common.cuh"
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <numeric>
 #include <thread>
@@ -302,6 +303,88 @@ void resolve_f32(const Prepared& P, const float* base, F32Weights* w) {
 }
 
 // --------------------------------------------------------------------------
+// bf16 decode weight stream: 34 SW128 tile images in consumption order
+// --------------------------------------------------------------------------
+uint16_t f2bf(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u) return (uint16_t)((u >> 16) | ((u & 0xFFFF) ? 0x40 : 0));
+  u += 0x7FFFu + ((u >> 16) & 1u);   // round to nearest even
+  return (uint16_t)(u >> 16);
+}
+
+// IEEE binary16, round to nearest even (overflow to inf, gradual underflow).
+uint16_t f2h(float f) {
+  uint32_t x;
+  std::memcpy(&x, &f, 4);
+  const uint32_t sign = (x >> 16) & 0x8000u;
+  const uint32_t e8 = (x >> 23) & 0xFFu;
+  uint32_t mant = x & 0x7FFFFFu;
+  if (e8 == 0xFFu) return (uint16_t)(sign | 0x7C00u | (mant ? 0x200u : 0u));
+  const int exp = (int)e8 - 127 + 15;
+  if (exp >= 31) return (uint16_t)(sign | 0x7C00u);
+  if (exp <= 0) {
+    if (exp < -10) return (uint16_t)sign;
+    mant |= 0x800000u;
+    const int shift = 14 - exp;
+    uint32_t h = mant >> shift;
+    const uint32_t rem = mant & ((1u << shift) - 1u), halfway = 1u << (shift - 1);
+    if (rem > halfway || (rem == halfway && (h & 1u))) ++h;
+    return (uint16_t)(sign | h);
+  }
+  uint32_t h = sign | ((uint32_t)exp << 10) | (mant >> 13);
+  const uint32_t rem = mant & 0x1FFFu;
+  if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;
+  return (uint16_t)h;
+}
+
+bool g_tile_f16 = true;   // operand format of the tiles being appended
+
+// Image of the 128 x 128 block W[r0:r0+128, k0:k0+128] (W row-major with
+// leading dimension ld) in the SW128 K-major layout of tcgen05.cuh.
+void append_tile(std::vector<uint16_t>& img, const float* W, int ld, int r0, int k0) {
+  const size_t base = img.size();
+  img.resize(base + 128 * 128);
+  for (int r = 0; r < 128; ++r)
+    for (int k = 0; k < 128; ++k) {
+      const int byte = (k >> 6) * 128 * 128 + (r >> 3) * 1024 + (r & 7) * 128 +
+                       ((((k & 63) >> 3) ^ (r & 7)) << 4) + (k & 7) * 2;
+      const float v = W[(size_t)(r0 + r) * ld + k0 + k];
+      img[base + byte / 2] = g_tile_f16 ? f2h(v) : f2bf(v);
+    }
+}
+
+bool build_stream_image(const std::map<std::string, TensorView>& t, bool f16,
+                        std::vector<uint16_t>* img) {
+  g_tile_f16 = f16;
+  auto get = [&](const std::string& n) -> const float* {
+    auto it = t.find(n);
+    return it == t.end() ? nullptr : it->second.data;
+  };
+  img->clear();
+  for (int l = 0; l < 3; ++l) {
+    const std::string p = "decoder_layers." + std::to_string(l) + ".";
+    const float* W1 = get(p + "W1.weight");
+    const float* W2 = get(p + "W2.weight");
+    const float* W3 = get(p + "W3.weight");
+    const float* Wi = get(p + "dense.W_in.weight");
+    const float* Wo = get(p + "dense.W_out.weight");
+    if (!W1 || !W2 || !W3 || !Wi || !Wo) return false;
+    if (l > 0) {
+      append_tile(*img, W1, 512, 0, 0);     // W1a: h_t block
+      append_tile(*img, W1, 512, 0, 384);   // W1d: h_j block
+    }
+    append_tile(*img, W2, 128, 0, 0);
+    append_tile(*img, W3, 128, 0, 0);
+    for (int i = 0; i < 4; ++i) {
+      append_tile(*img, Wi, 128, 128 * i, 0);   // W_in rows 128i..128i+127
+      append_tile(*img, Wo, 512, 0, 128 * i);   // W_out columns 128i..128i+127
+    }
+  }
+  return img->size() == (size_t)kStreamTilesPerStep * 128 * 128;
+}
+
+// --------------------------------------------------------------------------
 // Batch validation (algorithms/inverse_fold.cpp:232-261 semantics)
 // --------------------------------------------------------------------------
 bool finite_coords(const float* coords, const uint8_t* src, int64_t R) {
@@ -587,6 +670,68 @@ hkb_status decode_f32(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   return kOk;
 }
 
+hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
+                       const EncoderOut& eo, const DecoderTables& dt,
+                       const DeviceDesignOut& o) {
+  auto& ws = e->ws;
+  cudaStream_t st = e->stream;
+  const bool f16 = e->precision == HKB_PRECISION_F16;
+  const int64_t R = hb.R, SL = R * kK;
+  Bf16DecodeTables tb{};
+  for (int l = 0; l < 3; ++l) {
+    uint16_t* pe = ws.get_as<uint16_t>("b.PE" + std::to_string(l), SL * kH);
+    uint16_t* pv = ws.get_as<uint16_t>("b.PVenc" + std::to_string(l), R * kH);
+    if (!pe || !pv) return {HKB_UNAVAILABLE, "device allocation failed"};
+    convert_f32_to_16(st, dt.PE[l], pe, SL * kH, f16);
+    convert_f32_to_16(st, dt.PVenc[l], pv, R * kH, f16);
+    tb.PE[l] = pe;
+    tb.PVenc[l] = pv;
+  }
+  tb.Aenc0 = dt.Aenc0;
+  tb.h_enc = eo.h_v;
+  const int G = ar_tc_group_size();
+  std::vector<int> g0, gc;
+  for (int b = 0; b < hb.B; ++b)
+    for (int s = 0; s < hb.S[b]; s += G) {
+      g0.push_back(hb.seq_base[b] + s);
+      gc.push_back(std::min(G, hb.S[b] - s));
+    }
+  const int ng = (int)g0.size();
+  int* d_g0 = ws.get_as<int>("a.g0", ng);
+  int* d_gc = ws.get_as<int>("a.gc", ng);
+  int* pos = ws.get_as<int>("a.pos", hb.Q);
+  uint16_t* PV = ws.get_as<uint16_t>("b.PV", 2 * hb.Q * kH);
+  uint64_t* seeds = ws.get_as<uint64_t>("a.seed", hb.NS);
+  float* temps = ws.get_as<float>("a.temp", hb.NS);
+  if (!d_g0 || !d_gc || !pos || !PV || !seeds || !temps)
+    return {HKB_UNAVAILABLE, "device allocation failed"};
+  HKB_CUDA(cudaMemcpyAsync(d_g0, g0.data(), sizeof(int) * ng, cudaMemcpyHostToDevice, st));
+  HKB_CUDA(cudaMemcpyAsync(d_gc, gc.data(), sizeof(int) * ng, cudaMemcpyHostToDevice, st));
+  HKB_CUDA(cudaMemcpyAsync(seeds, hb.seq_seed.data(), sizeof(uint64_t) * hb.NS,
+                           cudaMemcpyHostToDevice, st));
+  HKB_CUDA(cudaMemcpyAsync(temps, hb.seq_temp.data(), sizeof(float) * hb.NS,
+                           cudaMemcpyHostToDevice, st));
+  HKB_CUDA(cudaMemsetAsync(PV, 0, sizeof(uint16_t) * 2 * hb.Q * kH, st));
+  ArBf16Args a{};
+  a.group_seq0 = d_g0;
+  a.group_count = d_gc;
+  a.num_groups = ng;
+  a.orders = o.orders;
+  a.pos = pos;
+  a.tokens = o.tokens;
+  a.log_probs = o.log_probs;
+  a.PV = PV;
+  a.seq_seed = seeds;
+  a.seq_temp = temps;
+  a.mask = eo.mask;
+  a.e_idx = eo.e_idx;
+  a.total_rows = hb.Q;
+  launch_ar_decode_tc(st, db.bv, e->wbf, tb, a, f16, e->d_err);
+  launch_scores(st, db.bv, o.tokens, o.log_probs, eo.mask, o.scores);
+  e->launches += 8;
+  return kOk;
+}
+
 hkb_status check_device_error(hkb_engine* e) {
   unsigned int h = 0;
   HKB_CUDA(cudaMemcpyAsync(&h, e->d_err, sizeof(unsigned int), cudaMemcpyDeviceToHost,
@@ -654,7 +799,8 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
   s = decoder_tables_f32(e, *hb, eo, &dt);
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[2], st));
-  s = decode_f32(e, *hb, db, eo, dt, out);
+  s = e->precision == HKB_PRECISION_FP32 ? decode_f32(e, *hb, db, eo, dt, out)
+                                          : decode_tc(e, *hb, db, eo, dt, out);
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[3], st));
   HKB_CUDA(cudaGetLastError());
@@ -681,10 +827,9 @@ hkb_status hkb_mpnn_create(const void* st_blob, size_t length, int device,
                            int32_t precision, hkb_engine** out) {
   if (out == nullptr) return invalid("engine output pointer is null");
   *out = nullptr;
-  if (precision != HKB_PRECISION_FP32 && precision != HKB_PRECISION_BF16)
-    return invalid("precision must be HKB_PRECISION_FP32 or HKB_PRECISION_BF16");
-  if (precision == HKB_PRECISION_BF16)
-    return {HKB_UNIMPLEMENTED, "bf16 tensor-core path is not built in this library"};
+  if (precision != HKB_PRECISION_FP32 && precision != HKB_PRECISION_BF16 &&
+      precision != HKB_PRECISION_F16)
+    return invalid("precision must be HKB_PRECISION_FP32, HKB_PRECISION_BF16 or HKB_PRECISION_F16");
   std::map<std::string, TensorView> tensors;
   std::vector<float> storage;
   const char* why = nullptr;
@@ -721,6 +866,37 @@ hkb_status hkb_mpnn_create(const void* st_blob, size_t length, int device,
     return internal("weight upload failed");
   }
   resolve_f32(P, static_cast<const float*>(e->d_weights), &e->w32);
+  std::vector<uint16_t> img;
+  if (!build_stream_image(tensors, precision == HKB_PRECISION_F16, &img)) {
+    hkb_mpnn_destroy(e);
+    return invalid("ProteinMPNN v_48_020 weights: missing decoder tensor");
+  }
+  if (cudaMalloc(&e->d_stream, img.size() * sizeof(uint16_t)) != cudaSuccess ||
+      cudaMemcpy(e->d_stream, img.data(), img.size() * sizeof(uint16_t),
+                 cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    hkb_mpnn_destroy(e);
+    return {HKB_UNAVAILABLE, "device allocation failed"};
+  }
+  {
+    Bf16DecodeWeights& W = e->wbf;
+    W.stream = static_cast<const unsigned char*>(e->d_stream);
+    for (int l = 0; l < 3; ++l) {
+      const auto& D = e->w32.dec[l];
+      W.Stab[l] = D.Stab;
+      W.b1[l] = D.b1;
+      W.b2[l] = D.b2;
+      W.b3[l] = D.b3;
+      W.n1w[l] = D.n1w;
+      W.n1b[l] = D.n1b;
+      W.n2w[l] = D.n2w;
+      W.n2b[l] = D.n2b;
+      W.bin[l] = D.bin;
+      W.bout[l] = D.bout;
+    }
+    W.headT = e->w32.headT;
+    W.head_b = e->w32.head_b;
+  }
   *out = e;
   return kOk;
 }
@@ -731,6 +907,7 @@ void hkb_mpnn_destroy(hkb_engine* e) {
   if (e->stream) cudaStreamSynchronize(e->stream);
   e->ws.release();
   if (e->d_weights) cudaFree(e->d_weights);
+  if (e->d_stream) cudaFree(e->d_stream);
   if (e->d_err) cudaFree(e->d_err);
   if (e->pinned) cudaFreeHost(e->pinned);
   for (auto& ev : e->ev)

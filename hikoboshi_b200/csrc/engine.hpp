@@ -75,6 +75,8 @@ struct hkb_engine {
   void* d_weights = nullptr;
   size_t weights_bytes = 0;
   hkb::F32Weights w32{};
+  void* d_stream = nullptr;          // bf16 decode weight tiles (SW128 images)
+  hkb::Bf16DecodeWeights wbf{};
   hkb::Workspace ws;
   unsigned int* d_err = nullptr;
   void* pinned = nullptr;

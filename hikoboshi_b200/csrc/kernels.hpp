@@ -155,6 +155,61 @@ void launch_ar_decode_f32(cudaStream_t st, const BatchView& bv,
 
 int ar_f32_group_size();
 
+// ---- bf16 tensor-core path --------------------------------------------------
+// Weight tiles for the fused decode kernel: every 128 x 128 operand tile is a
+// bf16 image already in the SW128 K-major shared-memory layout, and the tiles
+// sit in the exact order the kernel consumes them in one decode position:
+//   layer 0: W2, W3, (W_in[i], W_out[:, i]) for i = 0..3        (10 tiles)
+//   then for l = 1, 2: W1a_l, W1d_l, W2_l, W3_l, 4 x (W_in, W_out) (12 each)
+constexpr int kStreamTilesPerStep = 34;
+constexpr int kTileBytes = 128 * 128 * 2;
+
+struct Bf16DecodeWeights {
+  const unsigned char* stream;  // [34][32 KiB]
+  const float* Stab[3];         // [21,128] W1c_l . W_s
+  const float* b1[3];
+  const float* b2[3];
+  const float* b3[3];
+  const float* n1w[3];
+  const float* n1b[3];
+  const float* n2w[3];
+  const float* n2b[3];
+  const float* bin[3];   // [512]
+  const float* bout[3];
+  const float* headT;    // [128,21] fp32
+  const float* head_b;
+};
+
+struct Bf16DecodeTables {
+  const uint16_t* PE[3];     // bf16 [R*48,128]
+  const uint16_t* PVenc[3];  // bf16 [R,128]
+  const float* Aenc0;        // [R,128]
+  const float* h_enc;        // [R,128]
+};
+
+struct ArBf16Args {
+  const int* group_seq0;
+  const int* group_count;
+  int num_groups;
+  const int* orders;
+  int* pos;
+  int* tokens;
+  float* log_probs;
+  uint16_t* PV;              // bf16 [2,Q,128] (zeroed by the caller)
+  const uint64_t* seq_seed;
+  const float* seq_temp;
+  const float* mask;
+  const int* e_idx;
+  int64_t total_rows;
+};
+
+int ar_tc_group_size();
+// f32 -> fp16 (f16 = true) or bf16, round to nearest even.
+void convert_f32_to_16(cudaStream_t st, const float* src, uint16_t* dst, int64_t n, bool f16);
+void launch_ar_decode_tc(cudaStream_t st, const BatchView& bv,
+                         const Bf16DecodeWeights& w, const Bf16DecodeTables& t,
+                         const ArBf16Args& a, bool f16, unsigned int* err);
+
 void launch_scores(cudaStream_t st, const BatchView& bv, const int* tokens,
                    const float* log_probs, const float* mask, float* scores);
 

@@ -1,0 +1,660 @@
+// Tensor-core throughput path: the fused persistent autoregressive decode
+// kernel on tcgen05 tensor cores, with 16-bit operands (fp16 or bf16) and fp32
+// accumulation, LayerNorm and softmax.
+//
+// One CTA owns up to 16 sequences of one protein and walks all L decode
+// positions (inverse_fold_scalar.cpp:801-879).  Per position and DecLayer the
+// dense work is restated so that every contraction is a 128-row tcgen05 MMA
+// with the weights as the A operand (M = output features on TMEM lanes) and
+// the activations as the B operand (N = sequences or neighbour slots on TMEM
+// columns):
+//   node terms   D_A = W1a h,  D_PV = W1d h          M=128 N=16  K=128
+//   messages     D2  = W2 GELU(A_t + W1b h_E + ...)   M=128 N=96  K=128 (x8 chunks)
+//   aggregation  D3  = W3 (sum_k GELU(D2 + b2))       M=128 N=16  K=128
+//   FFN          DF  = W_in[i] h1,  DO += W_out[:, i] GELU(DF + b_in)  (i = 0..3)
+// The slot sum runs along a thread's own TMEM row, LayerNorm statistics are
+// warp reductions over a transposed fp32 copy, and the sampler is the
+// reference's (serial over 21 logits, double CDF).
+//
+// Weight tiles stream through a 3-slot shared-memory ring by 1-D bulk copies
+// (no tensor map) issued by thread 0 in consumption order; the neighbour-slot
+// operand is double-buffered so gathering chunk c+1 overlaps the MMA of chunk
+// c.  Every wait is bounded; a timeout sets the error word and the CTA stops.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "kernels.hpp"
+#include "tcgen05.cuh"
+
+namespace hkb {
+namespace {
+
+using namespace tc;
+
+constexpr int kGB = 16;           // sequences per CTA
+constexpr int kChunkSeqs = 2;     // sequences per message MMA
+constexpr int kChunkN = kChunkSeqs * kK;  // 96 neighbour slots
+constexpr int kSlots = 3;         // weight ring depth
+constexpr int kThreadsB = 256;
+
+// TMEM columns (fp32 accumulators, lanes = output features)
+constexpr uint32_t kColD2 = 0;    // 2 x 96
+constexpr uint32_t kColA = 192;
+constexpr uint32_t kColPV = 208;
+constexpr uint32_t kColD3 = 224;
+constexpr uint32_t kColDF = 240;
+constexpr uint32_t kColDO = 256;
+constexpr uint32_t kTmemCols = 512;
+
+// Shared memory map (offsets from a 1024-byte aligned base)
+constexpr uint32_t kOffW = 0;                                   // 3 x 32 KiB
+constexpr uint32_t kOffG1 = kOffW + kSlots * kTileBytes;        // 2 x 96 x 256 B
+constexpr uint32_t kG1Bytes = kChunkN * 256;
+constexpr uint32_t kOffHb = kOffG1 + 2 * kG1Bytes;              // [16,128] bf16
+constexpr uint32_t kOffSb = kOffHb + 4096;
+constexpr uint32_t kOffH1b = kOffSb + 4096;
+constexpr uint32_t kOffFb = kOffH1b + 4096;
+constexpr uint32_t kOffH = kOffFb + 4096;                       // fp32 [16,128]
+constexpr uint32_t kOffAa = kOffH + kGB * kH * 4;
+constexpr uint32_t kOffXs = kOffAa + kGB * kH * 4;
+constexpr uint32_t kOffNb = kOffXs + kGB * kH * 4;              // int [16,48]
+constexpr uint32_t kOffLogit = kOffNb + kGB * kK * 4;           // float [16,32]
+constexpr uint32_t kOffMisc = kOffLogit + kGB * 32 * 4;
+constexpr uint32_t kSmemBytes = kOffMisc + 1024 + 1024;         // + misc + alignment slack
+
+struct Misc {
+  uint64_t full[kSlots];
+  uint64_t bar_d2[2];
+  uint64_t bar_all;
+  uint32_t tbase;
+  int abort_flag;
+  int t[kGB];
+  float m[kGB];
+  long long qrow[kGB];
+  unsigned long long rng[kGB];
+  float temp[kGB];
+};
+static_assert(sizeof(Misc) <= 1024, "misc block");
+
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// GELU(x) ~= x/2 (1 + tanh(u(x))) with u an odd degree-5 polynomial fitted to
+// the exact erf form: max error 2.5e-5 with exact tanh, against 4.7e-4 for
+// the textbook cubic u, whose error is one-signed over wide ranges and so
+// accumulates through the 48-slot sums.  x is clamped to [-5, 5] inside u
+// (tanh(u) has saturated there).  tanh is the hardware tanh.approx.f32.  The
+// fp32 parity path uses the reference's erf form instead.
+__device__ __forceinline__ float gelu_tc(float x) {
+  const float hx = 0.5f * x;
+  const float xc = fminf(fmaxf(x, -5.0f), 5.0f);
+  const float x2 = xc * xc;
+  const float u = xc * fmaf(fmaf(-3.51516790e-04f, x2, 3.70056460e-02f), x2, 7.97507884e-01f);
+  return fmaf(hx, tanh_approx(u), hx);
+}
+
+template <bool F16>
+__device__ __forceinline__ uint32_t pack16(float a, float b) {
+  if constexpr (F16) {
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  } else {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
+}
+
+template <bool F16>
+__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (F16) {
+      const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      f[2 * i] = p.x;
+      f[2 * i + 1] = p.y;
+    } else {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  }
+}
+
+template <bool F16>
+__device__ __forceinline__ uint16_t to16(float a) {
+  return (uint16_t)(pack16<F16>(a, 0.0f) & 0xFFFFu);
+}
+
+// Instruction descriptor for fp16 (format 0) or bf16 (format 1) operands.
+template <bool F16>
+__host__ __device__ constexpr uint32_t idesc16(int M, int N) {
+  return F16 ? (idesc_bf16(M, N) & ~((7u << 7) | (7u << 10))) : idesc_bf16(M, N);
+}
+
+__device__ __forceinline__ unsigned long long splitmix_next(unsigned long long& s) {
+  unsigned long long z = (s += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Thread-0 state of the weight-tile stream.
+struct Stream {
+  long long issued;   // tiles whose loads were issued
+  long long used;     // tiles whose last MMA was issued
+  long long total;    // tiles this CTA consumes
+};
+
+__device__ __forceinline__ void stream_issue(Stream& s, unsigned char* sm, Misc& M,
+                                             const unsigned char* img) {
+  // Issue loads while a slot is free: tile j may load once tile j - kSlots is
+  // released (its MMAs complete, tracked by `used` after a commit wait).
+  while (s.issued < s.total && s.issued < s.used + kSlots) {
+    const int slot = (int)(s.issued % kSlots);
+    const int tile = (int)(s.issued % kStreamTilesPerStep);
+    mbar_arrive_expect_tx(&M.full[slot], kTileBytes);
+    bulk_g2s(sm + kOffW + slot * kTileBytes, img + (size_t)tile * kTileBytes, kTileBytes,
+             &M.full[slot]);
+    ++s.issued;
+  }
+}
+
+// Waits until tile `j` is resident; returns its shared address.
+__device__ __forceinline__ uint32_t stream_wait(long long j, unsigned char* sm, Misc& M,
+                                                unsigned int* err) {
+  const int slot = (int)(j % kSlots);
+  if (!mbar_wait(&M.full[slot], (uint32_t)((j / kSlots) & 1), err)) M.abort_flag = 1;
+  return smem_u32(sm + kOffW + slot * kTileBytes);
+}
+
+template <bool F16>
+__global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
+    BatchView bv, Bf16DecodeWeights w, Bf16DecodeTables tb, ArBf16Args a, unsigned int* err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  Misc& M = *reinterpret_cast<Misc*>(sm + kOffMisc);
+  float (*hS)[kH] = reinterpret_cast<float (*)[kH]>(sm + kOffH);
+  float (*Aa)[kH] = reinterpret_cast<float (*)[kH]>(sm + kOffAa);
+  float (*Xs)[kH] = reinterpret_cast<float (*)[kH]>(sm + kOffXs);
+  int (*Nb)[kK] = reinterpret_cast<int (*)[kK]>(sm + kOffNb);
+  float (*Lg)[32] = reinterpret_cast<float (*)[32]>(sm + kOffLogit);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3;             // TMEM lane quadrant
+  const int wg = warp >> 2;              // warpgroup 0 / 1
+  const int feat = quad * 32 + lane;     // output feature this thread reads
+  const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+
+  const int g = blockIdx.x;
+  const int seq0 = a.group_seq0[g];
+  const int n = a.group_count[g];
+  const int b = bv.seq_prot[seq0];
+  const int off = bv.prot_res_off[b];
+  const int L = bv.prot_len[b];
+  const int K = L < kK ? L : kK;
+
+  if (tid == 0) {
+    for (int i = 0; i < kSlots; ++i) mbar_init(&M.full[i], 1);
+    mbar_init(&M.bar_d2[0], 1);
+    mbar_init(&M.bar_d2[1], 1);
+    mbar_init(&M.bar_all, 1);
+    M.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (tid < kGB) {
+    const bool live = tid < n;
+    M.qrow[tid] = live ? bv.seq_row_off[seq0 + tid] : 0;
+    M.rng[tid] = live ? a.seq_seed[seq0 + tid] : 0ull;
+    M.temp[tid] = live ? a.seq_temp[seq0 + tid] : 1.0f;
+  }
+  // Zero the small operand tiles once (rows of absent sequences stay zero).
+  for (int e = tid; e < 4 * 4096 / 16; e += kThreadsB)
+    reinterpret_cast<uint4*>(sm + kOffHb)[e] = make_uint4(0, 0, 0, 0);
+  if (warp == 0) {
+    tmem_alloc(&M.tbase, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = M.tbase;   // TMEM base address
+
+  Stream st{0, 0, (long long)L * kStreamTilesPerStep};
+  if (tid == 0) stream_issue(st, sm, M, w.stream);
+
+  // decode positions of every residue of this CTA's sequences
+  for (int s = 0; s < n; ++s)
+    for (int p = tid; p < L; p += kThreadsB) {
+      const int t = a.orders[M.qrow[s] + p];
+      if (t < 0 || t >= L) {
+        atomicOr(err, kErrBadIndex);
+        continue;
+      }
+      a.pos[M.qrow[s] + t] = p;
+    }
+  __syncthreads();
+
+  uint32_t ph_d2[2] = {0, 0};
+  uint32_t ph_all = 0;
+  long long tile = 0;   // next tile to consume (same on all threads)
+
+  for (int p = 0; p < L; ++p) {
+    // uniform exit: every thread takes the same branch
+    if (__syncthreads_or(M.abort_flag)) break;
+    // ---- per-position set-up ------------------------------------------------
+    if (tid < kGB) {
+      int t = 0;
+      float m = 0.0f;
+      if (tid < n) {
+        t = a.orders[M.qrow[tid] + p];
+        t = (t < 0 || t >= L) ? 0 : t;
+        m = a.mask[off + t];
+      }
+      M.t[tid] = t;
+      M.m[tid] = m;
+    }
+    __syncthreads();
+    for (int e = tid; e < kGB * kH; e += kThreadsB) {
+      const int s = e >> 7, f = e & 127;
+      hS[s][f] = s < n ? tb.h_enc[(int64_t)(off + M.t[s]) * kH + f] : 0.0f;
+      Aa[s][f] = s < n ? tb.Aenc0[(int64_t)(off + M.t[s]) * kH + f] : 0.0f;
+    }
+    for (int e = tid; e < n * kK; e += kThreadsB) {
+      const int s = e / kK, k = e % kK;
+      int code = 0;
+      if (k < K) {
+        const int64_t rt = off + M.t[s];
+        int j = a.e_idx[rt * kK + k];
+        if (j < 0 || j >= L) {
+          atomicOr(err, kErrBadIndex);
+          j = M.t[s];
+        }
+        const int64_t qj = M.qrow[s] + j;
+        const bool bw = a.pos[qj] < p;
+        const int tok = bw ? a.tokens[qj] : 0;
+        code = j | (bw ? (1 << 16) : 0) | (tok << 17);
+      }
+      Nb[s][k] = code;
+    }
+    __syncthreads();
+
+    for (int l = 0; l < 3; ++l) {
+      if (__syncthreads_or(M.abort_flag)) break;
+      // ---- node terms for l >= 1 (MMAs issued at the end of layer l-1) -----
+      if (l > 0) {
+        if (!mbar_wait(&M.bar_all, ph_all, err)) M.abort_flag = 1;
+        ph_all ^= 1;
+        tc_fence_after();
+        if (tid == 0) {
+          st.used = tile;                       // W1a, W1d of this layer released
+          stream_issue(st, sm, M, w.stream);
+        }
+        float v[16];
+        if (wg == 0) {
+          tmem_ld16(tm + lane_base + kColA, v);
+          const float b1 = w.b1[l][feat];
+#pragma unroll
+          for (int s = 0; s < kGB; ++s) Aa[s][feat] = v[s] + b1;
+        } else {
+          tmem_ld16(tm + lane_base + kColPV, v);
+          uint16_t* PV = a.PV + (int64_t)(l - 1) * a.total_rows * kH;
+#pragma unroll
+          for (int s = 0; s < kGB; ++s)
+            if (s < n && M.m[s] != 0.0f)
+              PV[(M.qrow[s] + M.t[s]) * kH + feat] = to16<F16>(v[s]);
+        }
+        tc_fence_before();
+        __syncthreads();
+      }
+      // ---- messages: gather + GELU -> W2 MMA -> GELU + slot sum ------------
+      const uint16_t* PE = tb.PE[l];
+      const uint16_t* PVenc = tb.PVenc[l];
+      const uint16_t* PVl = l > 0 ? a.PV + (int64_t)(l - 1) * a.total_rows * kH : nullptr;
+      const float* Stab = w.Stab[l];
+      const int nch = (n + kChunkSeqs - 1) / kChunkSeqs;
+      auto gather = [&](int c) {
+        unsigned char* dst = sm + kOffG1 + (c & 1) * kG1Bytes;
+        for (int e = tid; e < kChunkN * 16; e += kThreadsB) {
+          const int r = e >> 4, c8 = e & 15;
+          const int s = c * kChunkSeqs + r / kK, k = r % kK;
+          uint4 outv = make_uint4(0, 0, 0, 0);
+          if (s < n && k < K) {
+            const int code = Nb[s][k];
+            const int j = code & 0xFFFF;
+            const bool bw = (code >> 16) & 1;
+            const int tok = code >> 17;
+            const int64_t rt = off + M.t[s];
+            float x[8], pe[8], pv[8];
+            const float4 a0 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2];
+            const float4 a1 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2 + 1];
+            unpack8<F16>(reinterpret_cast<const uint4*>(PE + (rt * kK + k) * kH)[c8], pe);
+            if (bw && l > 0)
+              unpack8<F16>(reinterpret_cast<const uint4*>(PVl + (M.qrow[s] + j) * kH)[c8], pv);
+            else
+              unpack8<F16>(reinterpret_cast<const uint4*>(PVenc + (int64_t)(off + j) * kH)[c8], pv);
+            x[0] = a0.x; x[1] = a0.y; x[2] = a0.z; x[3] = a0.w;
+            x[4] = a1.x; x[5] = a1.y; x[6] = a1.z; x[7] = a1.w;
+            if (bw) {
+              const float4 s0 = reinterpret_cast<const float4*>(Stab + tok * kH)[c8 * 2];
+              const float4 s1 = reinterpret_cast<const float4*>(Stab + tok * kH)[c8 * 2 + 1];
+              x[0] += s0.x; x[1] += s0.y; x[2] += s0.z; x[3] += s0.w;
+              x[4] += s1.x; x[5] += s1.y; x[6] += s1.z; x[7] += s1.w;
+            }
+            float y[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = gelu_tc(x[i] + pe[i] + pv[i]);
+            outv = make_uint4(pack16<F16>(y[0], y[1]), pack16<F16>(y[2], y[3]),
+                              pack16<F16>(y[4], y[5]), pack16<F16>(y[6], y[7]));
+          }
+          *reinterpret_cast<uint4*>(dst + sw128_offset(r, c8 * 8, kChunkN)) = outv;
+        }
+      };
+      const long long w2_tile = tile;
+      auto issue_w2 = [&](int c) {
+        if (tid == 0) {
+          const uint32_t wa = stream_wait(w2_tile, sm, M, err);
+          tc_fence_after();
+          if (!M.abort_flag)
+            mma_k128(tm + kColD2 + (c & 1) * kChunkN, wa,
+                     smem_u32(sm + kOffG1 + (c & 1) * kG1Bytes), kChunkN,
+                     idesc16<F16>(128, kChunkN), false);
+          mma_commit(&M.bar_d2[c & 1]);
+        }
+      };
+      gather(0);
+      fence_async_smem();
+      __syncthreads();
+      issue_w2(0);
+      for (int c = 0; c < nch; ++c) {
+        if (c + 1 < nch) {
+          gather(c + 1);
+          fence_async_smem();
+        }
+        __syncthreads();
+        if (c + 1 < nch) issue_w2(c + 1);
+        if (!mbar_wait(&M.bar_d2[c & 1], ph_d2[c & 1], err)) M.abort_flag = 1;
+        ph_d2[c & 1] ^= 1;
+        tc_fence_after();
+        // epilogue of chunk c: warpgroup wg takes sequence 2c + wg
+        {
+          const int s = c * kChunkSeqs + wg;
+          const float b2 = w.b2[l][feat];
+          float total = 0.0f;
+          const uint32_t col = kColD2 + (c & 1) * kChunkN + wg * kK;
+#pragma unroll
+          for (int q = 0; q < 3; ++q) {
+            float v[16];
+            tmem_ld16(tm + lane_base + col + q * 16, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (q * 16 + i < K) total += gelu_tc(v[i] + b2);
+          }
+          if (s < n)
+            *reinterpret_cast<uint16_t*>(sm + kOffSb + sw128_offset(s, feat, kGB)) =
+                to16<F16>(total);
+        }
+        tc_fence_before();
+        __syncthreads();
+      }
+      ++tile;                                   // W2 consumed
+      // ---- W3 after the slot sum, residual + LayerNorm 1 --------------------
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        st.used = tile;                         // W2's MMAs have completed
+        stream_issue(st, sm, M, w.stream);
+        const uint32_t wa = stream_wait(tile, sm, M, err);
+        tc_fence_after();
+        if (!M.abort_flag)
+          mma_k128(tm + kColD3, wa, smem_u32(sm + kOffSb), kGB, idesc16<F16>(128, kGB), false);
+        mma_commit(&M.bar_all);
+      }
+      ++tile;                                   // W3
+      if (!mbar_wait(&M.bar_all, ph_all, err)) M.abort_flag = 1;
+      ph_all ^= 1;
+      tc_fence_after();
+      if (tid == 0) {
+        st.used = tile;
+        stream_issue(st, sm, M, w.stream);
+      }
+      {
+        float v[16];
+        tmem_ld16(tm + lane_base + kColD3, v);
+        const float b3 = w.b3[l][feat] * (float)K;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int s = wg * 8 + q;
+          Xs[s][feat] = hS[s][feat] + (v[s] + b3) * (1.0f / kMessageScale);
+        }
+      }
+      tc_fence_before();
+      __syncthreads();
+      for (int s = warp; s < kGB; s += 8) {
+        float x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = Xs[s][lane * 4 + u];
+        warp_layer_norm128(x, w.n1w[l], w.n1b[l], lane);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) Xs[s][lane * 4 + u] = x[u];   // h1 (fp32)
+        uint2 pk = make_uint2(pack16<F16>(x[0], x[1]), pack16<F16>(x[2], x[3]));
+        *reinterpret_cast<uint2*>(sm + kOffH1b + sw128_offset(s, lane * 4, kGB)) = pk;
+      }
+      fence_async_smem();
+      __syncthreads();
+      // ---- FFN: DO = sum_i W_out[:, i] GELU(W_in[i] h1 + b_in[i]) ----------
+      for (int i = 0; i < 4; ++i) {
+        if (tid == 0) {
+          const uint32_t wa = stream_wait(tile, sm, M, err);
+          tc_fence_after();
+          if (!M.abort_flag)
+            mma_k128(tm + kColDF, wa, smem_u32(sm + kOffH1b), kGB, idesc16<F16>(128, kGB), false);
+          mma_commit(&M.bar_all);
+        }
+        ++tile;                                 // W_in[i]
+        if (!mbar_wait(&M.bar_all, ph_all, err)) M.abort_flag = 1;
+        ph_all ^= 1;
+        tc_fence_after();
+        if (tid == 0) {
+          st.used = tile;
+          stream_issue(st, sm, M, w.stream);
+        }
+        {
+          float v[16];
+          tmem_ld16(tm + lane_base + kColDF, v);
+          const float bi = w.bin[l][i * 128 + feat];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int s = wg * 8 + q;
+            const float y = s < n ? gelu_tc(v[s] + bi) : 0.0f;
+            *reinterpret_cast<uint16_t*>(sm + kOffFb + sw128_offset(s, feat, kGB)) = to16<F16>(y);
+          }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+          const uint32_t wa = stream_wait(tile, sm, M, err);
+          tc_fence_after();
+          if (!M.abort_flag)
+            mma_k128(tm + kColDO, wa, smem_u32(sm + kOffFb), kGB, idesc16<F16>(128, kGB), i > 0);
+        }
+        ++tile;                                 // W_out[:, i]
+      }
+      if (tid == 0) mma_commit(&M.bar_all);
+      if (!mbar_wait(&M.bar_all, ph_all, err)) M.abort_flag = 1;
+      ph_all ^= 1;
+      tc_fence_after();
+      if (tid == 0) {
+        st.used = tile;
+        stream_issue(st, sm, M, w.stream);
+      }
+      // ---- residual + LayerNorm 2, residue mask ------------------------------
+      {
+        float v[16];
+        tmem_ld16(tm + lane_base + kColDO, v);
+        const float bo = w.bout[l][feat];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int s = wg * 8 + q;
+          Aa[s][feat] = Xs[s][feat] + v[s] + bo;   // Aa reused as LN2 input
+        }
+      }
+      tc_fence_before();
+      __syncthreads();
+      for (int s = warp; s < kGB; s += 8) {
+        float x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = Aa[s][lane * 4 + u];
+        warp_layer_norm128(x, w.n2w[l], w.n2b[l], lane);
+        const float m = M.m[s];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          x[u] = (m == 1.0f) ? x[u] : x[u] * m;
+          hS[s][lane * 4 + u] = x[u];
+        }
+        uint2 pk = make_uint2(pack16<F16>(x[0], x[1]), pack16<F16>(x[2], x[3]));
+        *reinterpret_cast<uint2*>(sm + kOffHb + sw128_offset(s, lane * 4, kGB)) = pk;
+      }
+      fence_async_smem();
+      __syncthreads();
+      // ---- next layer's node terms: W1a h, W1d h ------------------------------
+      if (l < 2) {
+        if (tid == 0) {
+          uint32_t wa = stream_wait(tile, sm, M, err);
+          tc_fence_after();
+          if (!M.abort_flag)
+            mma_k128(tm + kColA, wa, smem_u32(sm + kOffHb), kGB, idesc16<F16>(128, kGB), false);
+          wa = stream_wait(tile + 1, sm, M, err);
+          tc_fence_after();
+          if (!M.abort_flag)
+            mma_k128(tm + kColPV, wa, smem_u32(sm + kOffHb), kGB, idesc16<F16>(128, kGB), false);
+          mma_commit(&M.bar_all);
+        }
+        tile += 2;                              // W1a, W1d of layer l+1 (released
+                                                // after the wait at its start)
+      }
+    }
+    if (__syncthreads_or(M.abort_flag)) break;
+    // ---- logits and sampling ------------------------------------------------
+    for (int e = tid; e < kGB * kV; e += kThreadsB) {
+      const int s = e / kV, v = e % kV;
+      float z = 0.0f;
+      if (s < n) {
+        z = w.head_b[v];
+#pragma unroll 8
+        for (int f = 0; f < kH; ++f) z = fmaf(hS[s][f], w.headT[f * kV + v], z);
+      }
+      Lg[s][v] = z;
+    }
+    __syncthreads();
+    if (lane == 0) {
+      for (int s = warp; s < n; s += 8) {
+        const int t = M.t[s];
+        const int64_t q = M.qrow[s] + t;
+        float* lp = a.log_probs + q * kV;
+        int tok = kV - 1;
+        if (M.m[s] == 0.0f) {
+          for (int v = 0; v < kV; ++v) lp[v] = 0.0f;
+        } else {
+          const float temperature = M.temp[s];
+          const bool greedy = !(temperature > 0.0f);
+          const float T = (temperature > 0.0f && isfinite(temperature)) ? temperature : 1.0f;
+          float zz[kV], prob[kV];
+          float mx = -INFINITY;
+          for (int v = 0; v < kV; ++v) {
+            zz[v] = Lg[s][v] / T;
+            mx = fmaxf(mx, zz[v]);
+          }
+          float sum = 0.0f;
+          for (int v = 0; v < kV; ++v) {
+            prob[v] = expf(zz[v] - mx);
+            sum += prob[v];
+          }
+          const float ls = logf(sum), inv = 1.0f / sum;
+          for (int v = 0; v < kV; ++v) {
+            prob[v] *= inv;
+            lp[v] = (zz[v] - mx) - ls;
+          }
+          if (greedy) {
+            tok = 0;
+            for (int v = 1; v < kV; ++v)
+              if (zz[v] > zz[tok]) tok = v;
+          } else {
+            unsigned long long r = M.rng[s];
+            const double u = (double)(splitmix_next(r) >> 11) * (1.0 / 9007199254740992.0);
+            M.rng[s] = r;
+            double cum = 0.0;
+            for (int v = 0; v < kV; ++v) {
+              cum += (double)prob[v];
+              if (u < cum) {
+                tok = v;
+                break;
+              }
+            }
+          }
+        }
+        a.tokens[q] = tok;
+      }
+    }
+    __syncthreads();
+  }
+  // Drain: no bulk copy may still be in flight when the CTA exits.
+  if (tid == 0) {
+    for (long long j = tile; j < st.issued; ++j) {
+      const int slot = (int)(j % kSlots);
+      mbar_wait(&M.full[slot], (uint32_t)((j / kSlots) & 1), err);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, kTmemCols);
+}
+
+template <bool F16>
+__global__ void f32_to_16_kernel(const float* __restrict__ src, uint16_t* __restrict__ dst,
+                                 int64_t n) {
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  if (i + 1 < n) {
+    *reinterpret_cast<uint32_t*>(dst + i) = pack16<F16>(src[i], src[i + 1]);
+  } else if (i < n) {
+    dst[i] = to16<F16>(src[i]);
+  }
+}
+
+}  // namespace
+
+int ar_tc_group_size() { return kGB; }
+
+void convert_f32_to_16(cudaStream_t st, const float* src, uint16_t* dst, int64_t n, bool f16) {
+  if (n <= 0) return;
+  const int64_t threads = (n + 1) / 2;
+  const unsigned grid = (unsigned)((threads + 255) / 256);
+  if (f16) f32_to_16_kernel<true><<<grid, 256, 0, st>>>(src, dst, n);
+  else f32_to_16_kernel<false><<<grid, 256, 0, st>>>(src, dst, n);
+}
+
+void launch_ar_decode_tc(cudaStream_t st, const BatchView& bv, const Bf16DecodeWeights& w,
+                         const Bf16DecodeTables& t, const ArBf16Args& a, bool f16,
+                         unsigned int* err) {
+  if (a.num_groups <= 0) return;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(ar_decode_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kSmemBytes);
+    cudaFuncSetAttribute(ar_decode_tc_kernel<false>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    attr_set = true;
+  }
+  if (f16)
+    ar_decode_tc_kernel<true><<<a.num_groups, kThreadsB, kSmemBytes, st>>>(bv, w, t, a, err);
+  else
+    ar_decode_tc_kernel<false><<<a.num_groups, kThreadsB, kSmemBytes, st>>>(bv, w, t, a, err);
+}
+
+}  // namespace hkb

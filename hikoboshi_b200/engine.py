@@ -75,7 +75,8 @@ class DesignEngine:
         self._lib = _lib.load()
         blob = weights if isinstance(weights, (bytes, bytearray)) else Path(weights).read_bytes()
         self._blob = ctypes.create_string_buffer(bytes(blob), len(blob))
-        prec = {"fp32": _lib.PRECISION_FP32, "bf16": _lib.PRECISION_BF16}[precision]
+        prec = {"fp32": _lib.PRECISION_FP32, "bf16": _lib.PRECISION_BF16,
+                "f16": _lib.PRECISION_F16}[precision]
         h = ctypes.c_void_p()
         check(self._lib.hkb_mpnn_create(self._blob, len(blob), device, prec, ctypes.byref(h)))
         self._h = h

@@ -53,8 +53,12 @@ typedef enum {
    * 1e-4 of the reference's fp32 log-probs. */
   HKB_PRECISION_FP32 = 0,
   /* bf16 weights/activations on tcgen05 tensor cores, fp32 accumulation,
-   * fp32 LayerNorm and softmax: the throughput mode. */
-  HKB_PRECISION_BF16 = 1
+   * fp32 LayerNorm and softmax. */
+  HKB_PRECISION_BF16 = 1,
+  /* fp16 weights/activations on tcgen05 tensor cores (same tensor-core rate
+   * as bf16, 8x finer rounding), fp32 accumulation, LayerNorm and softmax:
+   * the throughput mode. */
+  HKB_PRECISION_F16 = 2
 } hkb_precision;
 
 typedef enum {

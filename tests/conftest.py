@@ -58,6 +58,14 @@ def engine_fp32(weights_path):
 
 
 @pytest.fixture(scope="session")
+def engine_f16(weights_path):
+    from hikoboshi_b200 import DesignEngine
+    eng = DesignEngine(weights_path, device=0, precision="f16")
+    yield eng
+    eng.close()
+
+
+@pytest.fixture(scope="session")
 def engine_bf16(weights_path):
     from hikoboshi_b200 import DesignEngine
     eng = DesignEngine(weights_path, device=0, precision="bf16")
