@@ -367,6 +367,21 @@ def run_ours(args):
     return 0
 
 
+def run_profile_case(args):
+    """One untimed design on a smaller case (64 backbones x L=128 x 32
+    sequences, T=0.1) for ncu captures: the same kernels as the bench step
+    with about half the device footprint."""
+    from hikoboshi_b200 import DesignEngine, synthetic_backbone
+    bb = [synthetic_backbone(i, 128) for i in range(N_PROT)]
+    eng = DesignEngine(WEIGHTS, device=0, precision=args.precision)
+    eng.design([b[0] for b in bb], [b[1] for b in bb], num_seqs=N_SEQ, seeds=list(range(N_PROT)),
+               temperatures=TEMP, keep_log_probs=True)
+    print(json.dumps({"profile_case": "64 x L=128 x 32", "precision": args.precision,
+                      **eng.last_timings()}))
+    eng.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -375,7 +390,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", choices=["f16", "bf16", "fp32"], default="f16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="one untimed design on 64 x L=128 x 32 (for ncu captures)")
     args = ap.parse_args()
+    if args.profile_case:
+        return run_profile_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -384,6 +384,84 @@ bool build_stream_image(const std::map<std::string, TensorView>& t, bool f16,
   return img->size() == (size_t)kStreamTilesPerStep * 128 * 128;
 }
 
+// fp16 GEMM image of rows [r0, r0+nrows) and columns [c0, c0+K) of W
+// (row-major, leading dimension ld): [Kp/64 atoms][nrows x 64] SW128.
+void append_gemm_image(std::vector<uint16_t>& img, const float* W, int ld, int r0, int nrows,
+                       int c0, int K) {
+  const int Kp = (K + 63) & ~63;
+  const size_t base = img.size();
+  img.resize(base + (size_t)nrows * Kp, 0);
+  for (int r = 0; r < nrows; ++r)
+    for (int k = 0; k < K; ++k) {
+      const size_t byte = (size_t)(k >> 6) * nrows * 128 + (size_t)(r >> 3) * 1024 +
+                          (size_t)(r & 7) * 128 + (size_t)((((k & 63) >> 3) ^ (r & 7)) << 4) +
+                          (size_t)(k & 7) * 2;
+      img[base + byte / 2] = f2h(W[(size_t)(r0 + r) * ld + c0 + k]);
+    }
+}
+
+// All GEMM operands of the tensor-core encoder and decoder tables, by name.
+bool build_gemm_images(const std::map<std::string, TensorView>& t, std::vector<uint16_t>* img,
+                       std::map<std::string, size_t>* at) {
+  auto get = [&](const std::string& n) -> const float* {
+    auto it = t.find(n);
+    return it == t.end() ? nullptr : it->second.data;
+  };
+  auto mark = [&](const std::string& name) { (*at)[name] = img->size() * 2; };
+  const float* We = get("features.edge_embedding.weight");
+  const float* WeE = get("W_e.weight");
+  if (!We || !WeE) return false;
+  mark("edge");
+  append_gemm_image(*img, We, 416, 0, 128, 0, 416);
+  mark("W_e");
+  append_gemm_image(*img, WeE, 128, 0, 128, 0, 128);
+  for (int l = 0; l < 3; ++l) {
+    const std::string p = "encoder_layers." + std::to_string(l) + ".";
+    const std::string q = "enc" + std::to_string(l) + ".";
+    for (const char* nm : {"W1", "W11"}) {
+      const float* W = get(p + nm + ".weight");
+      if (!W) return false;
+      // [W1a ; W1c]: the h_i and h_j input blocks stacked as 256 output rows
+      std::vector<float> stack((size_t)256 * 128);
+      for (int r = 0; r < 128; ++r)
+        for (int k = 0; k < 128; ++k) {
+          stack[(size_t)r * 128 + k] = W[(size_t)r * 384 + k];
+          stack[(size_t)(128 + r) * 128 + k] = W[(size_t)r * 384 + 256 + k];
+        }
+      mark(q + nm + "ac");
+      append_gemm_image(*img, stack.data(), 128, 0, 256, 0, 128);
+      mark(q + nm + "b");
+      append_gemm_image(*img, W, 384, 0, 128, 128, 128);
+    }
+    for (const char* nm : {"W2", "W3", "W12", "W13"}) {
+      const float* W = get(p + nm + ".weight");
+      if (!W) return false;
+      mark(q + nm);
+      append_gemm_image(*img, W, 128, 0, 128, 0, 128);
+    }
+    const float* Wi = get(p + "dense.W_in.weight");
+    const float* Wo = get(p + "dense.W_out.weight");
+    if (!Wi || !Wo) return false;
+    mark(q + "Win");
+    append_gemm_image(*img, Wi, 128, 0, 512, 0, 128);
+    mark(q + "Wout");
+    append_gemm_image(*img, Wo, 512, 0, 128, 0, 512);
+  }
+  for (int l = 0; l < 3; ++l) {
+    const std::string p = "decoder_layers." + std::to_string(l) + ".";
+    const std::string q = "dec" + std::to_string(l) + ".";
+    const float* W1 = get(p + "W1.weight");
+    if (!W1) return false;
+    mark(q + "W1b");
+    append_gemm_image(*img, W1, 512, 0, 128, 128, 128);
+    mark(q + "W1d");
+    append_gemm_image(*img, W1, 512, 0, 128, 384, 128);
+    mark(q + "W1a");
+    append_gemm_image(*img, W1, 512, 0, 128, 0, 128);
+  }
+  return true;
+}
+
 // --------------------------------------------------------------------------
 // Batch validation (algorithms/inverse_fold.cpp:232-261 semantics)
 // --------------------------------------------------------------------------
@@ -527,11 +605,6 @@ hkb_status upload_tables(hkb_engine* e, const HostBatch& hb, DeviceBatch* db) {
 // --------------------------------------------------------------------------
 // Device pipeline (fp32)
 // --------------------------------------------------------------------------
-struct Launcher {
-  hkb_engine* e;
-  void count(int n = 1) { e->launches += n; }
-};
-
 hkb_status encode_f32(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
                       EncoderOut* eo) {
   auto& ws = e->ws;
@@ -586,6 +659,7 @@ hkb_status encode_f32(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
     launch_edge_ln_update(st, bv, G1, eo->e_idx, E.n3w, E.n3b, eo->h_e);
     n += 16;
   }
+  HKB_CUDA(cudaGetLastError());
   return kOk;
 }
 
@@ -609,6 +683,122 @@ hkb_status decoder_tables_f32(hkb_engine* e, const HostBatch& hb, const EncoderO
   gemm_f32(st, R, kH, kH, eo.h_v, kH, w.dec[0].W1aT, kH, w.dec[0].b1, 0, a0, kH);
   dt->Aenc0 = a0;
   e->launches += 7;
+  return kOk;
+}
+
+// Tensor-core encoder: the same pipeline as encode_f32 with every slot-sized
+// and node-sized contraction on tcgen05 (fp16 operands, fp32 accumulation,
+// fp32 intermediates); gathers, aggregation and LayerNorms stay as they are.
+hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
+                     EncoderOut* eo) {
+  auto& ws = e->ws;
+  cudaStream_t st = e->stream;
+  const F32Weights& w = e->w32;
+  const int64_t R = hb.R, SL = R * kK;
+  eo->e_idx = ws.get_as<int>("e.idx", SL);
+  eo->d2 = ws.get_as<float>("e.d2", SL);
+  eo->mask = ws.get_as<float>("e.mask", R);
+  eo->h_e = ws.get_as<float>("e.he", SL * kH);
+  eo->h_v = ws.get_as<float>("e.hv", R * kH);
+  float* feat = ws.get_as<float>("e.feat", SL * kEdgeIn);
+  float* E1 = ws.get_as<float>("e.s1", SL * kH);
+  float* EB = ws.get_as<float>("e.s2", SL * kH);
+  float* G1 = ws.get_as<float>("e.s3", SL * kH);
+  float* NAC = ws.get_as<float>("e.nac", R * 256);
+  float* Sv = ws.get_as<float>("e.S", R * kH);
+  float* cnt = ws.get_as<float>("e.cnt", R);
+  float* T3 = ws.get_as<float>("e.T3", R * kH);
+  float* h1 = ws.get_as<float>("e.h1", R * kH);
+  float* F = ws.get_as<float>("e.F", R * kFfn);
+  float* Y = ws.get_as<float>("e.Y", R * kH);
+  if (!eo->e_idx || !eo->d2 || !eo->mask || !eo->h_e || !eo->h_v || !feat || !E1 ||
+      !EB || !G1 || !NAC || !Sv || !cnt || !T3 || !h1 || !F || !Y)
+    return {HKB_UNAVAILABLE, "device allocation failed"};
+  const BatchView& bv = db.bv;
+  auto lin = [&](int64_t M, int N, int K, const void* A, int64_t lda, const char* img,
+                 const float* bias, int act, void* C, int64_t ldc, bool out_f16) {
+    LinearTcArgs p;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.A = A;
+    p.lda = lda;
+    p.W = e->gemm_img.at(img);
+    p.bias = bias;
+    p.act = act;
+    p.C = C;
+    p.ldc = ldc;
+    p.out_f16 = out_f16;
+    p.err = e->d_err;
+    launch_linear_tc(st, p, e->num_sms);
+    e->launches += 1;
+  };
+  launch_knn(st, bv, db.coords, db.sources, eo->e_idx, eo->d2, eo->mask, e->d_err, hb.max_len);
+  launch_edge_features(st, bv, w, db.coords, db.sources, eo->e_idx, feat);
+  e->launches += 2;
+  lin(SL, kH, kEdgeIn, feat, kEdgeIn, "edge", nullptr, 0, E1, kH, false);
+  launch_ln_rows(st, SL, E1, nullptr, nullptr, w.norm_e_w, w.norm_e_b, nullptr, nullptr, E1);
+  lin(SL, kH, kH, E1, kH, "W_e", w.We_b, 0, eo->h_e, kH, false);
+  HKB_CUDA(cudaMemsetAsync(eo->h_v, 0, sizeof(float) * R * kH, st));
+  e->launches += 1;
+  for (int l = 0; l < 3; ++l) {
+    const auto& E = w.enc[l];
+    const std::string q = "enc" + std::to_string(l) + ".";
+    lin(R, 256, kH, eo->h_v, kH, (q + "W1ac").c_str(), E.b1ac, 0, NAC, 256, false);
+    lin(SL, kH, kH, eo->h_e, kH, (q + "W1b").c_str(), nullptr, 0, EB, kH, false);
+    launch_enc_msg_in(st, bv, NAC, EB, eo->e_idx, G1);
+    lin(SL, kH, kH, G1, kH, (q + "W2").c_str(), E.b2, 1, EB, kH, false);
+    launch_enc_aggregate(st, bv, EB, eo->e_idx, eo->mask, Sv, cnt);
+    lin(R, kH, kH, Sv, kH, (q + "W3").c_str(), nullptr, 0, T3, kH, false);
+    launch_enc_node_update(st, bv, T3, cnt, E.b3, eo->h_v, E.n1w, E.n1b, h1);
+    lin(R, kFfn, kH, h1, kH, (q + "Win").c_str(), E.bin, 1, F, kFfn, false);
+    lin(R, kH, kFfn, F, kFfn, (q + "Wout").c_str(), nullptr, 0, Y, kH, false);
+    launch_ln_rows(st, R, h1, Y, E.bout, E.n2w, E.n2b, eo->mask, nullptr, eo->h_v);
+    lin(R, 256, kH, eo->h_v, kH, (q + "W11ac").c_str(), E.b11ac, 0, NAC, 256, false);
+    lin(SL, kH, kH, eo->h_e, kH, (q + "W11b").c_str(), nullptr, 0, EB, kH, false);
+    launch_enc_msg_in(st, bv, NAC, EB, eo->e_idx, G1);
+    lin(SL, kH, kH, G1, kH, (q + "W12").c_str(), E.b12, 1, EB, kH, false);
+    lin(SL, kH, kH, EB, kH, (q + "W13").c_str(), E.b13, 0, G1, kH, false);
+    launch_edge_ln_update(st, bv, G1, eo->e_idx, E.n3w, E.n3b, eo->h_e);
+    e->launches += 6;
+  }
+  HKB_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+// Decoder tables straight to 16-bit (fp16 mode) for the fused decode kernel.
+hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const EncoderOut& eo,
+                             Bf16DecodeTables* tb) {
+  auto& ws = e->ws;
+  cudaStream_t st = e->stream;
+  const int64_t R = hb.R, SL = R * kK;
+  for (int l = 0; l < 3; ++l) {
+    uint16_t* pe = ws.get_as<uint16_t>("b.PE" + std::to_string(l), SL * kH);
+    uint16_t* pv = ws.get_as<uint16_t>("b.PVenc" + std::to_string(l), R * kH);
+    if (!pe || !pv) return {HKB_UNAVAILABLE, "device allocation failed"};
+    const std::string q = "dec" + std::to_string(l) + ".";
+    LinearTcArgs p;
+    p.N = kH;
+    p.K = kH;
+    p.err = e->d_err;
+    p.out_f16 = true;
+    p.M = SL; p.A = eo.h_e; p.lda = kH; p.W = e->gemm_img.at(q + "W1b"); p.C = pe; p.ldc = kH;
+    launch_linear_tc(st, p, e->num_sms);
+    p.M = R; p.A = eo.h_v; p.W = e->gemm_img.at(q + "W1d"); p.C = pv;
+    launch_linear_tc(st, p, e->num_sms);
+    tb->PE[l] = pe;
+    tb->PVenc[l] = pv;
+  }
+  float* a0 = ws.get_as<float>("d.Aenc0", R * kH);
+  if (!a0) return {HKB_UNAVAILABLE, "device allocation failed"};
+  LinearTcArgs p;
+  p.M = R; p.N = kH; p.K = kH; p.A = eo.h_v; p.lda = kH; p.W = e->gemm_img.at("dec0.W1a");
+  p.bias = e->w32.dec[0].b1; p.C = a0; p.ldc = kH; p.err = e->d_err;
+  launch_linear_tc(st, p, e->num_sms);
+  tb->Aenc0 = a0;
+  tb->h_enc = eo.h_v;
+  e->launches += 7;
+  HKB_CUDA(cudaGetLastError());
   return kOk;
 }
 
@@ -670,25 +860,33 @@ hkb_status decode_f32(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   return kOk;
 }
 
-hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
-                       const EncoderOut& eo, const DecoderTables& dt,
-                       const DeviceDesignOut& o) {
+// bf16 mode: the fp32 decoder tables rounded to bf16.
+hkb_status decoder_tables_bf16(hkb_engine* e, const HostBatch& hb, const EncoderOut& eo,
+                               const DecoderTables& dt, Bf16DecodeTables* tb) {
   auto& ws = e->ws;
   cudaStream_t st = e->stream;
-  const bool f16 = e->precision == HKB_PRECISION_F16;
   const int64_t R = hb.R, SL = R * kK;
-  Bf16DecodeTables tb{};
   for (int l = 0; l < 3; ++l) {
     uint16_t* pe = ws.get_as<uint16_t>("b.PE" + std::to_string(l), SL * kH);
     uint16_t* pv = ws.get_as<uint16_t>("b.PVenc" + std::to_string(l), R * kH);
     if (!pe || !pv) return {HKB_UNAVAILABLE, "device allocation failed"};
-    convert_f32_to_16(st, dt.PE[l], pe, SL * kH, f16);
-    convert_f32_to_16(st, dt.PVenc[l], pv, R * kH, f16);
-    tb.PE[l] = pe;
-    tb.PVenc[l] = pv;
+    convert_f32_to_16(st, dt.PE[l], pe, SL * kH, false);
+    convert_f32_to_16(st, dt.PVenc[l], pv, R * kH, false);
+    tb->PE[l] = pe;
+    tb->PVenc[l] = pv;
   }
-  tb.Aenc0 = dt.Aenc0;
-  tb.h_enc = eo.h_v;
+  tb->Aenc0 = dt.Aenc0;
+  tb->h_enc = eo.h_v;
+  e->launches += 6;
+  return kOk;
+}
+
+hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
+                     const EncoderOut& eo, const Bf16DecodeTables& tb,
+                     const DeviceDesignOut& o) {
+  auto& ws = e->ws;
+  cudaStream_t st = e->stream;
+  const bool f16 = e->precision == HKB_PRECISION_F16;
   const int G = ar_tc_group_size();
   std::vector<int> g0, gc;
   for (int b = 0; b < hb.B; ++b)
@@ -728,7 +926,7 @@ hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   a.total_rows = hb.Q;
   launch_ar_decode_tc(st, db.bv, e->wbf, tb, a, f16, e->d_err);
   launch_scores(st, db.bv, o.tokens, o.log_probs, eo.mask, o.scores);
-  e->launches += 8;
+  e->launches += 2;
   return kOk;
 }
 
@@ -743,19 +941,6 @@ hkb_status check_device_error(hkb_engine* e) {
   return kOk;
 }
 
-void* pinned(hkb_engine* e, size_t bytes) {
-  if (e->pinned_bytes < bytes) {
-    if (e->pinned) cudaFreeHost(e->pinned);
-    e->pinned = nullptr;
-    e->pinned_bytes = 0;
-    if (cudaMallocHost(&e->pinned, bytes) != cudaSuccess) {
-      cudaGetLastError();
-      return nullptr;
-    }
-    e->pinned_bytes = bytes;
-  }
-  return e->pinned;
-}
 
 hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
                          const uint8_t* host_src, const float* d_coords,
@@ -792,15 +977,25 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
                            cudaMemcpyHostToDevice, st));
   HKB_CUDA(cudaEventRecord(e->ev[0], st));
   EncoderOut eo;
-  s = encode_f32(e, *hb, db, &eo);
+  // fp32: SIMT parity pipeline; bf16: fp32 encoder, tables rounded to bf16;
+  // f16: tensor-core encoder writing fp16 tables.
+  const bool tc_encoder = e->precision == HKB_PRECISION_F16;
+  s = tc_encoder ? encode_tc(e, *hb, db, &eo) : encode_f32(e, *hb, db, &eo);
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[1], st));
   DecoderTables dt{};
-  s = decoder_tables_f32(e, *hb, eo, &dt);
+  Bf16DecodeTables tb{};
+  if (tc_encoder) {
+    s = decoder_tables_tc(e, *hb, eo, &tb);
+  } else {
+    s = decoder_tables_f32(e, *hb, eo, &dt);
+    if (s.code == HKB_OK && e->precision == HKB_PRECISION_BF16)
+      s = decoder_tables_bf16(e, *hb, eo, dt, &tb);
+  }
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[2], st));
   s = e->precision == HKB_PRECISION_FP32 ? decode_f32(e, *hb, db, eo, dt, out)
-                                          : decode_tc(e, *hb, db, eo, dt, out);
+                                          : decode_tc(e, *hb, db, eo, tb, out);
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[3], st));
   HKB_CUDA(cudaGetLastError());
@@ -879,6 +1074,24 @@ hkb_status hkb_mpnn_create(const void* st_blob, size_t length, int device,
     return {HKB_UNAVAILABLE, "device allocation failed"};
   }
   {
+    std::vector<uint16_t> gimg;
+    std::map<std::string, size_t> gat;
+    if (!build_gemm_images(tensors, &gimg, &gat)) {
+      hkb_mpnn_destroy(e);
+      return invalid("ProteinMPNN v_48_020 weights: missing tensor");
+    }
+    if (cudaMalloc(&e->d_gemm, gimg.size() * sizeof(uint16_t)) != cudaSuccess ||
+        cudaMemcpy(e->d_gemm, gimg.data(), gimg.size() * sizeof(uint16_t),
+                   cudaMemcpyHostToDevice) != cudaSuccess) {
+      cudaGetLastError();
+      hkb_mpnn_destroy(e);
+      return {HKB_UNAVAILABLE, "device allocation failed"};
+    }
+    for (const auto& kv : gat)
+      e->gemm_img[kv.first] = static_cast<const unsigned char*>(e->d_gemm) + kv.second;
+    e->num_sms = prop.multiProcessorCount;
+  }
+  {
     Bf16DecodeWeights& W = e->wbf;
     W.stream = static_cast<const unsigned char*>(e->d_stream);
     for (int l = 0; l < 3; ++l) {
@@ -908,8 +1121,8 @@ void hkb_mpnn_destroy(hkb_engine* e) {
   e->ws.release();
   if (e->d_weights) cudaFree(e->d_weights);
   if (e->d_stream) cudaFree(e->d_stream);
+  if (e->d_gemm) cudaFree(e->d_gemm);
   if (e->d_err) cudaFree(e->d_err);
-  if (e->pinned) cudaFreeHost(e->pinned);
   for (auto& ev : e->ev)
     if (ev) cudaEventDestroy(ev);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -1201,13 +1414,16 @@ static hkb_status single_protein_encode(hkb_engine* e, int32_t L, const float* c
   db->sources = d_src;
   s = upload_tables(e, *hb, db);
   if (s.code != HKB_OK) return s;
-  if (full) return encode_f32(e, *hb, *db, eo);
+  if (full)
+    return e->precision == HKB_PRECISION_F16 ? encode_tc(e, *hb, *db, eo)
+                                             : encode_f32(e, *hb, *db, eo);
   eo->e_idx = e->ws.get_as<int>("e.idx", (size_t)L * kK);
   eo->d2 = e->ws.get_as<float>("e.d2", (size_t)L * kK);
   eo->mask = e->ws.get_as<float>("e.mask", L);
   if (!eo->e_idx || !eo->d2 || !eo->mask) return {HKB_UNAVAILABLE, "device allocation failed"};
   launch_knn(st, db->bv, d_coords, d_src, eo->e_idx, eo->d2, eo->mask, e->d_err, L);
   e->launches += 1;
+  HKB_CUDA(cudaGetLastError());
   return kOk;
 }
 

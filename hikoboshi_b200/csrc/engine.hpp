@@ -75,12 +75,13 @@ struct hkb_engine {
   void* d_weights = nullptr;
   size_t weights_bytes = 0;
   hkb::F32Weights w32{};
-  void* d_stream = nullptr;          // bf16 decode weight tiles (SW128 images)
+  void* d_stream = nullptr;          // 16-bit decode weight tiles (SW128 images)
   hkb::Bf16DecodeWeights wbf{};
+  void* d_gemm = nullptr;            // fp16 GEMM weight images (tensor-core modes)
+  std::map<std::string, const unsigned char*> gemm_img;
+  int num_sms = 148;
   hkb::Workspace ws;
   unsigned int* d_err = nullptr;
-  void* pinned = nullptr;
-  size_t pinned_bytes = 0;
   int64_t launches = 0;
   float timings[4] = {0, 0, 0, 0};
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};

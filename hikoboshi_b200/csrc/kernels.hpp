@@ -203,6 +203,28 @@ struct ArBf16Args {
   int64_t total_rows;
 };
 
+// Persistent tcgen05 GEMM C[M,N] = act(A[M,K] W[N,K]^T + bias): A fp32 or fp16
+// (row-major), W an fp16 SW128 image laid out [K/64 atoms][N rows x 64]
+// (K padded to a multiple of 64), fp32 accumulation in TMEM, output fp32 or
+// fp16.  N in {128, 256, 384, 512}, K <= 512.
+struct LinearTcArgs {
+  int64_t M = 0;
+  int N = 0;
+  int K = 0;
+  const void* A = nullptr;
+  int64_t lda = 0;
+  bool a_f16 = false;
+  const unsigned char* W = nullptr;
+  const float* bias = nullptr;
+  int act = 0;          // 0 none, 1 GELU (erf form)
+  void* C = nullptr;
+  int64_t ldc = 0;
+  bool out_f16 = false;
+  unsigned int* err = nullptr;
+};
+size_t linear_tc_smem_bytes(int N, int K);
+void launch_linear_tc(cudaStream_t st, const LinearTcArgs& p, int num_sms);
+
 int ar_tc_group_size();
 // f32 -> fp16 (f16 = true) or bf16, round to nearest even.
 void convert_f32_to_16(cudaStream_t st, const float* src, uint16_t* dst, int64_t n, bool f16);

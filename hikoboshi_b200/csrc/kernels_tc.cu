@@ -60,7 +60,9 @@ constexpr uint32_t kOffAa = kOffH + kGB * kH * 4;
 constexpr uint32_t kOffXs = kOffAa + kGB * kH * 4;
 constexpr uint32_t kOffNb = kOffXs + kGB * kH * 4;              // int [16,48]
 constexpr uint32_t kOffLogit = kOffNb + kGB * kK * 4;           // float [16,32]
-constexpr uint32_t kOffMisc = kOffLogit + kGB * 32 * 4;
+constexpr uint32_t kOffStab = kOffLogit + kGB * 32 * 4;         // 16-bit [3,21,128]
+constexpr uint32_t kOffHead = kOffStab + 16384;                 // fp32 [128,21]
+constexpr uint32_t kOffMisc = kOffHead + kH * kV * 4;
 constexpr uint32_t kSmemBytes = kOffMisc + 1024 + 1024;         // + misc + alignment slack
 
 struct Misc {
@@ -182,6 +184,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   float (*Xs)[kH] = reinterpret_cast<float (*)[kH]>(sm + kOffXs);
   int (*Nb)[kK] = reinterpret_cast<int (*)[kK]>(sm + kOffNb);
   float (*Lg)[32] = reinterpret_cast<float (*)[32]>(sm + kOffLogit);
+  uint16_t* StabS = reinterpret_cast<uint16_t*>(sm + kOffStab);
+  float* HeadS = reinterpret_cast<float*>(sm + kOffHead);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -215,6 +219,12 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   // Zero the small operand tiles once (rows of absent sequences stay zero).
   for (int e = tid; e < 4 * 4096 / 16; e += kThreadsB)
     reinterpret_cast<uint4*>(sm + kOffHb)[e] = make_uint4(0, 0, 0, 0);
+  // Per-layer W1c.W_s table (16-bit) and the logit head (fp32) stay resident.
+  for (int e = tid; e < 3 * kV * kH; e += kThreadsB) {
+    const int l = e / (kV * kH), r = e % (kV * kH);
+    StabS[e] = to16<F16>(w.Stab[l][r]);
+  }
+  for (int e = tid; e < kH * kV; e += kThreadsB) HeadS[e] = w.headT[e];
   if (warp == 0) {
     tmem_alloc(&M.tbase, kTmemCols);
     tmem_relinquish();
@@ -315,39 +325,59 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       const uint16_t* PE = tb.PE[l];
       const uint16_t* PVenc = tb.PVenc[l];
       const uint16_t* PVl = l > 0 ? a.PV + (int64_t)(l - 1) * a.total_rows * kH : nullptr;
-      const float* Stab = w.Stab[l];
+      const uint16_t* StabL = StabS + l * kV * kH;
       const int nch = (n + kChunkSeqs - 1) / kChunkSeqs;
+      // Neighbour-slot operand of chunk c: a thread owns one 8-feature column
+      // chunk (tid % 16) of six slot rows; all twelve row loads are issued
+      // before any is consumed so their latencies overlap.
       auto gather = [&](int c) {
         unsigned char* dst = sm + kOffG1 + (c & 1) * kG1Bytes;
-        for (int e = tid; e < kChunkN * 16; e += kThreadsB) {
-          const int r = e >> 4, c8 = e & 15;
+        constexpr int kRowsPerThread = kChunkN / 16;
+        const int c8 = tid & 15;
+        const int r0 = tid >> 4;
+        uint4 pe_raw[kRowsPerThread], v_raw[kRowsPerThread];
+#pragma unroll
+        for (int i = 0; i < kRowsPerThread; ++i) {
+          const int r = r0 + 16 * i;
           const int s = c * kChunkSeqs + r / kK, k = r % kK;
-          uint4 outv = make_uint4(0, 0, 0, 0);
+          pe_raw[i] = make_uint4(0, 0, 0, 0);
+          v_raw[i] = make_uint4(0, 0, 0, 0);
           if (s < n && k < K) {
             const int code = Nb[s][k];
             const int j = code & 0xFFFF;
             const bool bw = (code >> 16) & 1;
-            const int tok = code >> 17;
             const int64_t rt = off + M.t[s];
-            float x[8], pe[8], pv[8];
+            pe_raw[i] = __ldg(reinterpret_cast<const uint4*>(PE + (rt * kK + k) * kH) + c8);
+            if (bw && l > 0)   // written by this kernel: coherent load
+              v_raw[i] = reinterpret_cast<const uint4*>(PVl + (M.qrow[s] + j) * kH)[c8];
+            else
+              v_raw[i] = __ldg(reinterpret_cast<const uint4*>(PVenc + (int64_t)(off + j) * kH) + c8);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kRowsPerThread; ++i) {
+          const int r = r0 + 16 * i;
+          const int s = c * kChunkSeqs + r / kK, k = r % kK;
+          uint4 outv = make_uint4(0, 0, 0, 0);
+          if (s < n && k < K) {
+            const int code = Nb[s][k];
+            const bool bw = (code >> 16) & 1;
+            const int tok = code >> 17;
+            float pe[8], pv[8], st[8];
+            unpack8<F16>(pe_raw[i], pe);
+            unpack8<F16>(v_raw[i], pv);
             const float4 a0 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2];
             const float4 a1 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2 + 1];
-            unpack8<F16>(reinterpret_cast<const uint4*>(PE + (rt * kK + k) * kH)[c8], pe);
-            if (bw && l > 0)
-              unpack8<F16>(reinterpret_cast<const uint4*>(PVl + (M.qrow[s] + j) * kH)[c8], pv);
-            else
-              unpack8<F16>(reinterpret_cast<const uint4*>(PVenc + (int64_t)(off + j) * kH)[c8], pv);
-            x[0] = a0.x; x[1] = a0.y; x[2] = a0.z; x[3] = a0.w;
-            x[4] = a1.x; x[5] = a1.y; x[6] = a1.z; x[7] = a1.w;
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
             if (bw) {
-              const float4 s0 = reinterpret_cast<const float4*>(Stab + tok * kH)[c8 * 2];
-              const float4 s1 = reinterpret_cast<const float4*>(Stab + tok * kH)[c8 * 2 + 1];
-              x[0] += s0.x; x[1] += s0.y; x[2] += s0.z; x[3] += s0.w;
-              x[4] += s1.x; x[5] += s1.y; x[6] += s1.z; x[7] += s1.w;
+              unpack8<F16>(reinterpret_cast<const uint4*>(StabL + tok * kH)[c8], st);
+            } else {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) st[q] = 0.0f;
             }
             float y[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) y[i] = gelu_tc(x[i] + pe[i] + pv[i]);
+            for (int q = 0; q < 8; ++q) y[q] = gelu_tc(av[q] + pe[q] + pv[q] + st[q]);
             outv = make_uint4(pack16<F16>(y[0], y[1]), pack16<F16>(y[2], y[3]),
                               pack16<F16>(y[4], y[5]), pack16<F16>(y[6], y[7]));
           }
@@ -386,14 +416,11 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           const float b2 = w.b2[l][feat];
           float total = 0.0f;
           const uint32_t col = kColD2 + (c & 1) * kChunkN + wg * kK;
+          float v[48];
+          tmem_ld48(tm + lane_base + col, v);
 #pragma unroll
-          for (int q = 0; q < 3; ++q) {
-            float v[16];
-            tmem_ld16(tm + lane_base + col + q * 16, v);
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (q * 16 + i < K) total += gelu_tc(v[i] + b2);
-          }
+          for (int i = 0; i < 48; ++i)
+            if (i < K) total += gelu_tc(v[i] + b2);
           if (s < n)
             *reinterpret_cast<uint16_t*>(sm + kOffSb + sw128_offset(s, feat, kGB)) =
                 to16<F16>(total);
@@ -547,7 +574,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       if (s < n) {
         z = w.head_b[v];
 #pragma unroll 8
-        for (int f = 0; f < kH; ++f) z = fmaf(hS[s][f], w.headT[f * kV + v], z);
+        for (int f = 0; f < kH; ++f) z = fmaf(hS[s][f], HeadS[f * kV + v], z);
       }
       Lg[s][v] = z;
     }
