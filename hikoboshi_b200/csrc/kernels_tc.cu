@@ -249,6 +249,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     }
   __syncthreads();
 
+  constexpr int kRowsPerThread = kChunkN / 16;
+  uint4 raw_pe[kRowsPerThread], raw_v[kRowsPerThread];   // in-flight slot rows
   uint32_t ph_d2[2] = {0, 0};
   uint32_t ph_all = 0;
   long long tile = 0;   // next tile to consume (same on all threads)
@@ -293,6 +295,76 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     }
     __syncthreads();
 
+    // Row loads of one neighbour-slot chunk: a thread owns one 8-feature column
+    // chunk (tid % 16) of six slot rows (W1b h_E row and the neighbour's
+    // W1d h row, fp16).
+    auto load_rows = [&](int c, int layer, uint4 (&pe_raw)[kRowsPerThread],
+                         uint4 (&v_raw)[kRowsPerThread]) {
+      const int c8 = tid & 15;
+      const int r0 = tid >> 4;
+      const uint16_t* PE = tb.PE[layer];
+      const uint16_t* PVenc = tb.PVenc[layer];
+      const uint16_t* PVl =
+          layer > 0 ? a.PV + (int64_t)(layer - 1) * a.total_rows * kH : nullptr;
+#pragma unroll
+      for (int i = 0; i < kRowsPerThread; ++i) {
+        const int r = r0 + 16 * i;
+        const int s = c * kChunkSeqs + r / kK, k = r % kK;
+        pe_raw[i] = make_uint4(0, 0, 0, 0);
+        v_raw[i] = make_uint4(0, 0, 0, 0);
+        if (s < n && k < K) {
+          const int code = Nb[s][k];
+          const int j = code & 0xFFFF;
+          const bool bw = (code >> 16) & 1;
+          const int64_t rt = off + M.t[s];
+          pe_raw[i] = __ldg(reinterpret_cast<const uint4*>(PE + (rt * kK + k) * kH) + c8);
+          if (bw && layer > 0)   // written by this kernel: coherent load
+            v_raw[i] = reinterpret_cast<const uint4*>(PVl + (M.qrow[s] + j) * kH)[c8];
+          else
+            v_raw[i] = __ldg(reinterpret_cast<const uint4*>(PVenc + (int64_t)(off + j) * kH) + c8);
+        }
+      }
+    };
+    // GELU(A_t + W1b h_E + V + W1c W_s[tok]) into the SW128 operand of chunk c.
+    auto build_operand = [&](int c, int layer, const uint16_t* StabL,
+                             const uint4 (&pe_raw)[kRowsPerThread],
+                             const uint4 (&v_raw)[kRowsPerThread]) {
+      unsigned char* dst = sm + kOffG1 + (c & 1) * kG1Bytes;
+      const int c8 = tid & 15;
+      const int r0 = tid >> 4;
+#pragma unroll
+      for (int i = 0; i < kRowsPerThread; ++i) {
+        const int r = r0 + 16 * i;
+        const int s = c * kChunkSeqs + r / kK, k = r % kK;
+        uint4 outv = make_uint4(0, 0, 0, 0);
+        if (s < n && k < K) {
+          const int code = Nb[s][k];
+          const bool bw = (code >> 16) & 1;
+          const int tok = code >> 17;
+          float pe[8], pv[8], st[8];
+          unpack8<F16>(pe_raw[i], pe);
+          unpack8<F16>(v_raw[i], pv);
+          const float4 a0 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2];
+          const float4 a1 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2 + 1];
+          const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+          if (bw) {
+            unpack8<F16>(reinterpret_cast<const uint4*>(StabL + tok * kH)[c8], st);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) st[q] = 0.0f;
+          }
+          float y[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) y[q] = gelu_tc(av[q] + pe[q] + pv[q] + st[q]);
+          outv = make_uint4(pack16<F16>(y[0], y[1]), pack16<F16>(y[2], y[3]),
+                            pack16<F16>(y[4], y[5]), pack16<F16>(y[6], y[7]));
+        }
+        *reinterpret_cast<uint4*>(dst + sw128_offset(r, c8 * 8, kChunkN)) = outv;
+      }
+      (void)layer;
+    };
+    load_rows(0, 0, raw_pe, raw_v);      // chunk 0 of layer 0
+
     for (int l = 0; l < 3; ++l) {
       if (__syncthreads_or(M.abort_flag)) break;
       // ---- node terms for l >= 1 (MMAs issued at the end of layer l-1) -----
@@ -325,65 +397,12 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       const uint16_t* PE = tb.PE[l];
       const uint16_t* PVenc = tb.PVenc[l];
       const uint16_t* PVl = l > 0 ? a.PV + (int64_t)(l - 1) * a.total_rows * kH : nullptr;
-      const uint16_t* StabL = StabS + l * kV * kH;
+      // Slot phase, software-pipelined one chunk deep: the row loads of chunk
+      // c+1 are issued right after chunk c's operand is built, so they land
+      // while chunk c's MMA and chunk c-1's epilogue run (and chunk 0 of the
+      // next layer is fetched during this layer's W3 / FFN phases).
       const int nch = (n + kChunkSeqs - 1) / kChunkSeqs;
-      // Neighbour-slot operand of chunk c: a thread owns one 8-feature column
-      // chunk (tid % 16) of six slot rows; all twelve row loads are issued
-      // before any is consumed so their latencies overlap.
-      auto gather = [&](int c) {
-        unsigned char* dst = sm + kOffG1 + (c & 1) * kG1Bytes;
-        constexpr int kRowsPerThread = kChunkN / 16;
-        const int c8 = tid & 15;
-        const int r0 = tid >> 4;
-        uint4 pe_raw[kRowsPerThread], v_raw[kRowsPerThread];
-#pragma unroll
-        for (int i = 0; i < kRowsPerThread; ++i) {
-          const int r = r0 + 16 * i;
-          const int s = c * kChunkSeqs + r / kK, k = r % kK;
-          pe_raw[i] = make_uint4(0, 0, 0, 0);
-          v_raw[i] = make_uint4(0, 0, 0, 0);
-          if (s < n && k < K) {
-            const int code = Nb[s][k];
-            const int j = code & 0xFFFF;
-            const bool bw = (code >> 16) & 1;
-            const int64_t rt = off + M.t[s];
-            pe_raw[i] = __ldg(reinterpret_cast<const uint4*>(PE + (rt * kK + k) * kH) + c8);
-            if (bw && l > 0)   // written by this kernel: coherent load
-              v_raw[i] = reinterpret_cast<const uint4*>(PVl + (M.qrow[s] + j) * kH)[c8];
-            else
-              v_raw[i] = __ldg(reinterpret_cast<const uint4*>(PVenc + (int64_t)(off + j) * kH) + c8);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < kRowsPerThread; ++i) {
-          const int r = r0 + 16 * i;
-          const int s = c * kChunkSeqs + r / kK, k = r % kK;
-          uint4 outv = make_uint4(0, 0, 0, 0);
-          if (s < n && k < K) {
-            const int code = Nb[s][k];
-            const bool bw = (code >> 16) & 1;
-            const int tok = code >> 17;
-            float pe[8], pv[8], st[8];
-            unpack8<F16>(pe_raw[i], pe);
-            unpack8<F16>(v_raw[i], pv);
-            const float4 a0 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2];
-            const float4 a1 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2 + 1];
-            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-            if (bw) {
-              unpack8<F16>(reinterpret_cast<const uint4*>(StabL + tok * kH)[c8], st);
-            } else {
-#pragma unroll
-              for (int q = 0; q < 8; ++q) st[q] = 0.0f;
-            }
-            float y[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) y[q] = gelu_tc(av[q] + pe[q] + pv[q] + st[q]);
-            outv = make_uint4(pack16<F16>(y[0], y[1]), pack16<F16>(y[2], y[3]),
-                              pack16<F16>(y[4], y[5]), pack16<F16>(y[6], y[7]));
-          }
-          *reinterpret_cast<uint4*>(dst + sw128_offset(r, c8 * 8, kChunkN)) = outv;
-        }
-      };
+      const uint16_t* StabL = StabS + l * kV * kH;
       const long long w2_tile = tile;
       auto issue_w2 = [&](int c) {
         if (tid == 0) {
@@ -396,38 +415,34 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           mma_commit(&M.bar_d2[c & 1]);
         }
       };
-      gather(0);
-      fence_async_smem();
-      __syncthreads();
-      issue_w2(0);
-      for (int c = 0; c < nch; ++c) {
-        if (c + 1 < nch) {
-          gather(c + 1);
-          fence_async_smem();
-        }
-        __syncthreads();
-        if (c + 1 < nch) issue_w2(c + 1);
+      auto epilogue = [&](int c) {
         if (!mbar_wait(&M.bar_d2[c & 1], ph_d2[c & 1], err)) M.abort_flag = 1;
         ph_d2[c & 1] ^= 1;
         tc_fence_after();
-        // epilogue of chunk c: warpgroup wg takes sequence 2c + wg
-        {
-          const int s = c * kChunkSeqs + wg;
-          const float b2 = w.b2[l][feat];
-          float total = 0.0f;
-          const uint32_t col = kColD2 + (c & 1) * kChunkN + wg * kK;
-          float v[48];
-          tmem_ld48(tm + lane_base + col, v);
+        const int s = c * kChunkSeqs + wg;      // warpgroup wg takes sequence 2c + wg
+        const float b2 = w.b2[l][feat];
+        float total = 0.0f;
+        float v[48];
+        tmem_ld48(tm + lane_base + kColD2 + (c & 1) * kChunkN + wg * kK, v);
 #pragma unroll
-          for (int i = 0; i < 48; ++i)
-            if (i < K) total += gelu_tc(v[i] + b2);
-          if (s < n)
-            *reinterpret_cast<uint16_t*>(sm + kOffSb + sw128_offset(s, feat, kGB)) =
-                to16<F16>(total);
-        }
+        for (int i = 0; i < 48; ++i)
+          if (i < K) total += gelu_tc(v[i] + b2);
+        if (s < n)
+          *reinterpret_cast<uint16_t*>(sm + kOffSb + sw128_offset(s, feat, kGB)) =
+              to16<F16>(total);
         tc_fence_before();
         __syncthreads();
+      };
+      for (int c = 0; c < nch; ++c) {
+        build_operand(c, l, StabL, raw_pe, raw_v);
+        fence_async_smem();
+        __syncthreads();
+        issue_w2(c);
+        if (c + 1 < nch) load_rows(c + 1, l, raw_pe, raw_v);
+        else if (l < 2) load_rows(0, l + 1, raw_pe, raw_v);
+        if (c >= 1) epilogue(c - 1);
       }
+      epilogue(nch - 1);
       ++tile;                                   // W2 consumed
       // ---- W3 after the slot sum, residual + LayerNorm 1 --------------------
       fence_async_smem();
