@@ -17,9 +17,14 @@
 // reference's (serial over 21 logits, double CDF).
 //
 // Weight tiles stream through a 3-slot shared-memory ring by 1-D bulk copies
-// (no tensor map) issued by thread 0 in consumption order; the neighbour-slot
-// operand is double-buffered so gathering chunk c+1 overlaps the MMA of chunk
-// c.  Every wait is bounded; a timeout sets the error word and the CTA stops.
+// (no tensor map) issued by thread 0 in consumption order.  The CTA has 16
+// warps.  In the message (slot) phase they split into 8 producer warps, which
+// gather neighbour rows (one chunk ahead, in registers), build the GELU
+// operand and issue the MMA, and 8 epilogue warps, which sum GELU(D2 + b2)
+// over the slots; the roles hand buffers to each other through mbarriers, so
+// the two GELU passes of consecutive chunks overlap.  All 16 warps share the
+// node, LayerNorm, FFN and sampling phases.  Every wait is bounded; a timeout
+// sets the error word and the CTA stops.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -36,7 +41,11 @@ constexpr int kGB = 16;           // sequences per CTA
 constexpr int kChunkSeqs = 2;     // sequences per message MMA
 constexpr int kChunkN = kChunkSeqs * kK;  // 96 neighbour slots
 constexpr int kSlots = 3;         // weight ring depth
-constexpr int kThreadsB = 256;
+constexpr int kThreadsB = 512;
+constexpr int kWarpsB = kThreadsB / 32;
+constexpr int kProducerWarps = 8;  // warps 0-7: slot gather, operand build, MMA issue
+constexpr int kProducerThreads = kProducerWarps * 32;
+// warps 8-15: slot-sum epilogue (two warps per TMEM lane quadrant)
 
 // TMEM columns (fp32 accumulators, lanes = output features)
 constexpr uint32_t kColD2 = 0;    // 2 x 96
@@ -67,7 +76,8 @@ constexpr uint32_t kSmemBytes = kOffMisc + 1024 + 1024;         // + misc + alig
 
 struct Misc {
   uint64_t full[kSlots];
-  uint64_t bar_d2[2];
+  uint64_t bar_d2[2];     // message MMA of a chunk complete (D2 buffer full)
+  uint64_t bar_free[2];   // epilogue warps done reading a D2 buffer
   uint64_t bar_all;
   uint32_t tbase;
   int abort_flag;
@@ -169,7 +179,8 @@ __device__ __forceinline__ void stream_issue(Stream& s, unsigned char* sm, Misc&
 __device__ __forceinline__ uint32_t stream_wait(long long j, unsigned char* sm, Misc& M,
                                                 unsigned int* err) {
   const int slot = (int)(j % kSlots);
-  if (!mbar_wait(&M.full[slot], (uint32_t)((j / kSlots) & 1), err)) M.abort_flag = 1;
+  if (!mbar_wait(&M.full[slot], (uint32_t)((j / kSlots) & 1), err))
+    *reinterpret_cast<volatile int*>(&M.abort_flag) = 1;
   return smem_u32(sm + kOffW + slot * kTileBytes);
 }
 
@@ -190,7 +201,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3;             // TMEM lane quadrant
-  const int wg = warp >> 2;              // warpgroup 0 / 1
+  const int wg = warp >> 2;              // warpgroup 0..3
   const int feat = quad * 32 + lane;     // output feature this thread reads
   const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
 
@@ -206,6 +217,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     for (int i = 0; i < kSlots; ++i) mbar_init(&M.full[i], 1);
     mbar_init(&M.bar_d2[0], 1);
     mbar_init(&M.bar_d2[1], 1);
+    mbar_init(&M.bar_free[0], kWarpsB - kProducerWarps);
+    mbar_init(&M.bar_free[1], kWarpsB - kProducerWarps);
     mbar_init(&M.bar_all, 1);
     M.abort_flag = 0;
     fence_barrier_init();
@@ -250,8 +263,10 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   __syncthreads();
 
   constexpr int kRowsPerThread = kChunkN / 16;
-  uint4 raw_pe[kRowsPerThread], raw_v[kRowsPerThread];   // in-flight slot rows
-  uint32_t ph_d2[2] = {0, 0};
+  const bool producer = warp < kProducerWarps;
+  volatile int* abort_p = &M.abort_flag;
+  uint4 raw_pe[kRowsPerThread], raw_v[kRowsPerThread];   // in-flight slot rows (producers)
+  uint32_t buf_use[2] = {0, 0};   // chunks issued on each D2 / operand buffer so far
   uint32_t ph_all = 0;
   long long tile = 0;   // next tile to consume (same on all threads)
 
@@ -295,9 +310,9 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     }
     __syncthreads();
 
-    // Row loads of one neighbour-slot chunk: a thread owns one 8-feature column
-    // chunk (tid % 16) of six slot rows (W1b h_E row and the neighbour's
-    // W1d h row, fp16).
+    // Row loads of one neighbour-slot chunk (producer threads): a thread owns
+    // one 8-feature column chunk (tid % 16) of six slot rows (W1b h_E row and
+    // the neighbour's W1d h row, 16-bit).
     auto load_rows = [&](int c, int layer, uint4 (&pe_raw)[kRowsPerThread],
                          uint4 (&v_raw)[kRowsPerThread]) {
       const int c8 = tid & 15;
@@ -326,7 +341,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       }
     };
     // GELU(A_t + W1b h_E + V + W1c W_s[tok]) into the SW128 operand of chunk c.
-    auto build_operand = [&](int c, int layer, const uint16_t* StabL,
+    auto build_operand = [&](int c, const uint16_t* StabL,
                              const uint4 (&pe_raw)[kRowsPerThread],
                              const uint4 (&v_raw)[kRowsPerThread]) {
       unsigned char* dst = sm + kOffG1 + (c & 1) * kG1Bytes;
@@ -361,103 +376,124 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         }
         *reinterpret_cast<uint4*>(dst + sw128_offset(r, c8 * 8, kChunkN)) = outv;
       }
-      (void)layer;
     };
-    load_rows(0, 0, raw_pe, raw_v);      // chunk 0 of layer 0
+    if (producer) load_rows(0, 0, raw_pe, raw_v);      // chunk 0 of layer 0
 
     for (int l = 0; l < 3; ++l) {
       if (__syncthreads_or(M.abort_flag)) break;
       // ---- node terms for l >= 1 (MMAs issued at the end of layer l-1) -----
       if (l > 0) {
-        if (!mbar_wait(&M.bar_all, ph_all, err)) M.abort_flag = 1;
+        if (!mbar_wait(&M.bar_all, ph_all, err)) *abort_p = 1;
         ph_all ^= 1;
         tc_fence_after();
         if (tid == 0) {
           st.used = tile;                       // W1a, W1d of this layer released
           stream_issue(st, sm, M, w.stream);
         }
-        float v[16];
-        if (wg == 0) {
-          tmem_ld16(tm + lane_base + kColA, v);
+        // warpgroups 0/1: A columns 0-7 / 8-15; warpgroups 2/3: PV columns
+        float v[8];
+        const int s0 = (wg & 1) * 8;
+        if (wg < 2) {
+          tmem_ld8(tm + lane_base + kColA + s0, v);
           const float b1 = w.b1[l][feat];
 #pragma unroll
-          for (int s = 0; s < kGB; ++s) Aa[s][feat] = v[s] + b1;
+          for (int q = 0; q < 8; ++q) Aa[s0 + q][feat] = v[q] + b1;
         } else {
-          tmem_ld16(tm + lane_base + kColPV, v);
+          tmem_ld8(tm + lane_base + kColPV + s0, v);
           uint16_t* PV = a.PV + (int64_t)(l - 1) * a.total_rows * kH;
 #pragma unroll
-          for (int s = 0; s < kGB; ++s)
-            if (s < n && M.m[s] != 0.0f)
-              PV[(M.qrow[s] + M.t[s]) * kH + feat] = to16<F16>(v[s]);
+          for (int q = 0; q < 8; ++q) {
+            const int s = s0 + q;
+            if (s < n && M.m[s] != 0.0f) PV[(M.qrow[s] + M.t[s]) * kH + feat] = to16<F16>(v[q]);
+          }
         }
         tc_fence_before();
         __syncthreads();
       }
       // ---- messages: gather + GELU -> W2 MMA -> GELU + slot sum ------------
-      const uint16_t* PE = tb.PE[l];
-      const uint16_t* PVenc = tb.PVenc[l];
-      const uint16_t* PVl = l > 0 ? a.PV + (int64_t)(l - 1) * a.total_rows * kH : nullptr;
-      // Slot phase, software-pipelined one chunk deep: the row loads of chunk
-      // c+1 are issued right after chunk c's operand is built, so they land
-      // while chunk c's MMA and chunk c-1's epilogue run (and chunk 0 of the
-      // next layer is fetched during this layer's W3 / FFN phases).
+      // Producer warps build chunk c's operand (rows prefetched into registers
+      // one chunk ahead; chunk 0 of the next layer is fetched during this
+      // layer's W3 / FFN phases) and issue its MMA; epilogue warps sum
+      // GELU(D2 + b2) over the slots of chunk c-1 meanwhile.  Two D2 / operand
+      // buffers; bar_d2 hands a full D2 to the epilogue (and frees the operand
+      // buffer), bar_free hands the D2 buffer back.
       const int nch = (n + kChunkSeqs - 1) / kChunkSeqs;
-      const uint16_t* StabL = StabS + l * kV * kH;
-      const long long w2_tile = tile;
-      auto issue_w2 = [&](int c) {
-        if (tid == 0) {
-          const uint32_t wa = stream_wait(w2_tile, sm, M, err);
-          tc_fence_after();
-          if (!M.abort_flag)
-            mma_k128(tm + kColD2 + (c & 1) * kChunkN, wa,
-                     smem_u32(sm + kOffG1 + (c & 1) * kG1Bytes), kChunkN,
-                     idesc16<F16>(128, kChunkN), false);
-          mma_commit(&M.bar_d2[c & 1]);
+      if (producer) {
+        const uint16_t* StabL = StabS + l * kV * kH;
+        uint32_t wa = 0;
+        for (int c = 0; c < nch; ++c) {
+          const int bf = c & 1;
+          // operand buffer bf is free once the MMA that last read it completed
+          if (buf_use[bf] > 0 && !*abort_p &&
+              !mbar_wait_abortable(&M.bar_d2[bf], (buf_use[bf] - 1) & 1, err, abort_p))
+            *abort_p = 1;
+          build_operand(c, StabL, raw_pe, raw_v);
+          fence_async_smem();
+          named_bar_sync(1, kProducerThreads);
+          if (tid == 0) {
+            if (c == 0) wa = stream_wait(tile, sm, M, err);
+            if (buf_use[bf] > 0 && !*abort_p &&
+                !mbar_wait_abortable(&M.bar_free[bf], (buf_use[bf] - 1) & 1, err, abort_p))
+              *abort_p = 1;
+            tc_fence_after();
+            if (!*abort_p)
+              mma_k128(tm + kColD2 + bf * kChunkN, wa,
+                       smem_u32(sm + kOffG1 + bf * kG1Bytes), kChunkN,
+                       idesc16<F16>(128, kChunkN), false);
+            mma_commit(&M.bar_d2[bf]);
+          }
+          ++buf_use[bf];
+          if (c + 1 < nch) load_rows(c + 1, l, raw_pe, raw_v);
+          else if (l < 2) load_rows(0, l + 1, raw_pe, raw_v);
         }
-      };
-      auto epilogue = [&](int c) {
-        if (!mbar_wait(&M.bar_d2[c & 1], ph_d2[c & 1], err)) M.abort_flag = 1;
-        ph_d2[c & 1] ^= 1;
-        tc_fence_after();
-        const int s = c * kChunkSeqs + wg;      // warpgroup wg takes sequence 2c + wg
+      } else {
+        const int sub = (warp - kProducerWarps) >> 2;   // sequence of the chunk
         const float b2 = w.b2[l][feat];
-        float total = 0.0f;
-        float v[48];
-        tmem_ld48(tm + lane_base + kColD2 + (c & 1) * kChunkN + wg * kK, v);
+        for (int c = 0; c < nch; ++c) {
+          const int bf = c & 1;
+          if (!*abort_p && !mbar_wait_abortable(&M.bar_d2[bf], buf_use[bf] & 1, err, abort_p))
+            *abort_p = 1;
+          ++buf_use[bf];
+          tc_fence_after();
+          const int s = c * kChunkSeqs + sub;
+          float total = 0.0f;
+          {
+            float v[32];
+            tmem_ld32(tm + lane_base + kColD2 + bf * kChunkN + sub * kK, v);
 #pragma unroll
-        for (int i = 0; i < 48; ++i)
-          if (i < K) total += gelu_tc(v[i] + b2);
-        if (s < n)
-          *reinterpret_cast<uint16_t*>(sm + kOffSb + sw128_offset(s, feat, kGB)) =
-              to16<F16>(total);
-        tc_fence_before();
-        __syncthreads();
-      };
-      for (int c = 0; c < nch; ++c) {
-        build_operand(c, l, StabL, raw_pe, raw_v);
-        fence_async_smem();
-        __syncthreads();
-        issue_w2(c);
-        if (c + 1 < nch) load_rows(c + 1, l, raw_pe, raw_v);
-        else if (l < 2) load_rows(0, l + 1, raw_pe, raw_v);
-        if (c >= 1) epilogue(c - 1);
+            for (int i = 0; i < 32; ++i)
+              if (i < K) total += gelu_tc(v[i] + b2);
+          }
+          {
+            float v[16];
+            tmem_ld16(tm + lane_base + kColD2 + bf * kChunkN + sub * kK + 32, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (i + 32 < K) total += gelu_tc(v[i] + b2);
+          }
+          if (s < n)
+            *reinterpret_cast<uint16_t*>(sm + kOffSb + sw128_offset(s, feat, kGB)) =
+                to16<F16>(total);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&M.bar_free[bf]);
+        }
+        fence_async_smem();                     // slot sums feed the W3 MMA
       }
-      epilogue(nch - 1);
       ++tile;                                   // W2 consumed
-      // ---- W3 after the slot sum, residual + LayerNorm 1 --------------------
-      fence_async_smem();
       __syncthreads();
+      // ---- W3 after the slot sum, residual + LayerNorm 1 --------------------
       if (tid == 0) {
         st.used = tile;                         // W2's MMAs have completed
         stream_issue(st, sm, M, w.stream);
         const uint32_t wa = stream_wait(tile, sm, M, err);
         tc_fence_after();
-        if (!M.abort_flag)
+        if (!*abort_p)
           mma_k128(tm + kColD3, wa, smem_u32(sm + kOffSb), kGB, idesc16<F16>(128, kGB), false);
         mma_commit(&M.bar_all);
       }
       ++tile;                                   // W3
-      if (!mbar_wait(&M.bar_all, ph_all, err)) M.abort_flag = 1;
+      if (!mbar_wait(&M.bar_all, ph_all, err)) *abort_p = 1;
       ph_all ^= 1;
       tc_fence_after();
       if (tid == 0) {
@@ -465,18 +501,18 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         stream_issue(st, sm, M, w.stream);
       }
       {
-        float v[16];
-        tmem_ld16(tm + lane_base + kColD3, v);
+        float v[4];
+        tmem_ld4(tm + lane_base + kColD3 + wg * 4, v);
         const float b3 = w.b3[l][feat] * (float)K;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int s = wg * 8 + q;
-          Xs[s][feat] = hS[s][feat] + (v[s] + b3) * (1.0f / kMessageScale);
+        for (int q = 0; q < 4; ++q) {
+          const int s = wg * 4 + q;
+          Xs[s][feat] = hS[s][feat] + (v[q] + b3) * (1.0f / kMessageScale);
         }
       }
       tc_fence_before();
       __syncthreads();
-      for (int s = warp; s < kGB; s += 8) {
+      for (int s = warp; s < kGB; s += kWarpsB) {
         float x[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) x[u] = Xs[s][lane * 4 + u];
@@ -493,12 +529,12 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         if (tid == 0) {
           const uint32_t wa = stream_wait(tile, sm, M, err);
           tc_fence_after();
-          if (!M.abort_flag)
+          if (!*abort_p)
             mma_k128(tm + kColDF, wa, smem_u32(sm + kOffH1b), kGB, idesc16<F16>(128, kGB), false);
           mma_commit(&M.bar_all);
         }
         ++tile;                                 // W_in[i]
-        if (!mbar_wait(&M.bar_all, ph_all, err)) M.abort_flag = 1;
+        if (!mbar_wait(&M.bar_all, ph_all, err)) *abort_p = 1;
         ph_all ^= 1;
         tc_fence_after();
         if (tid == 0) {
@@ -506,13 +542,13 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           stream_issue(st, sm, M, w.stream);
         }
         {
-          float v[16];
-          tmem_ld16(tm + lane_base + kColDF, v);
+          float v[4];
+          tmem_ld4(tm + lane_base + kColDF + wg * 4, v);
           const float bi = w.bin[l][i * 128 + feat];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const int s = wg * 8 + q;
-            const float y = s < n ? gelu_tc(v[s] + bi) : 0.0f;
+          for (int q = 0; q < 4; ++q) {
+            const int s = wg * 4 + q;
+            const float y = s < n ? gelu_tc(v[q] + bi) : 0.0f;
             *reinterpret_cast<uint16_t*>(sm + kOffFb + sw128_offset(s, feat, kGB)) = to16<F16>(y);
           }
         }
@@ -522,13 +558,13 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         if (tid == 0) {
           const uint32_t wa = stream_wait(tile, sm, M, err);
           tc_fence_after();
-          if (!M.abort_flag)
+          if (!*abort_p)
             mma_k128(tm + kColDO, wa, smem_u32(sm + kOffFb), kGB, idesc16<F16>(128, kGB), i > 0);
         }
         ++tile;                                 // W_out[:, i]
       }
       if (tid == 0) mma_commit(&M.bar_all);
-      if (!mbar_wait(&M.bar_all, ph_all, err)) M.abort_flag = 1;
+      if (!mbar_wait(&M.bar_all, ph_all, err)) *abort_p = 1;
       ph_all ^= 1;
       tc_fence_after();
       if (tid == 0) {
@@ -537,18 +573,18 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       }
       // ---- residual + LayerNorm 2, residue mask ------------------------------
       {
-        float v[16];
-        tmem_ld16(tm + lane_base + kColDO, v);
+        float v[4];
+        tmem_ld4(tm + lane_base + kColDO + wg * 4, v);
         const float bo = w.bout[l][feat];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int s = wg * 8 + q;
-          Aa[s][feat] = Xs[s][feat] + v[s] + bo;   // Aa reused as LN2 input
+        for (int q = 0; q < 4; ++q) {
+          const int s = wg * 4 + q;
+          Aa[s][feat] = Xs[s][feat] + v[q] + bo;   // Aa reused as LN2 input
         }
       }
       tc_fence_before();
       __syncthreads();
-      for (int s = warp; s < kGB; s += 8) {
+      for (int s = warp; s < kGB; s += kWarpsB) {
         float x[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) x[u] = Aa[s][lane * 4 + u];
@@ -569,11 +605,11 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         if (tid == 0) {
           uint32_t wa = stream_wait(tile, sm, M, err);
           tc_fence_after();
-          if (!M.abort_flag)
+          if (!*abort_p)
             mma_k128(tm + kColA, wa, smem_u32(sm + kOffHb), kGB, idesc16<F16>(128, kGB), false);
           wa = stream_wait(tile + 1, sm, M, err);
           tc_fence_after();
-          if (!M.abort_flag)
+          if (!*abort_p)
             mma_k128(tm + kColPV, wa, smem_u32(sm + kOffHb), kGB, idesc16<F16>(128, kGB), false);
           mma_commit(&M.bar_all);
         }
@@ -594,54 +630,51 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       Lg[s][v] = z;
     }
     __syncthreads();
-    if (lane == 0) {
-      for (int s = warp; s < n; s += 8) {
-        const int t = M.t[s];
-        const int64_t q = M.qrow[s] + t;
-        float* lp = a.log_probs + q * kV;
-        int tok = kV - 1;
-        if (M.m[s] == 0.0f) {
-          for (int v = 0; v < kV; ++v) lp[v] = 0.0f;
+    // One warp per sequence, one lane per vocabulary entry
+    // (sampler_scalar.cpp:49-92): temperature-scaled log-softmax emitted as
+    // the log-prob row, then greedy argmax (first maximum) or one uniform draw
+    // against the double-precision CDF.  Sums run as warp reductions, so they
+    // differ from the serial order by rounding only.
+    for (int s = warp; s < n; s += kWarpsB) {
+      const int t = M.t[s];
+      const int64_t q = M.qrow[s] + t;
+      float* lp = a.log_probs + q * kV;
+      const bool in_vocab = lane < kV;
+      int tok = kV - 1;
+      if (M.m[s] == 0.0f) {
+        if (in_vocab) lp[lane] = 0.0f;
+      } else {
+        const float temperature = M.temp[s];
+        const bool greedy = !(temperature > 0.0f);
+        const float T = (temperature > 0.0f && isfinite(temperature)) ? temperature : 1.0f;
+        const float z = in_vocab ? Lg[s][lane] / T : -INFINITY;
+        const float mx = warp_max(z);
+        const float e = in_vocab ? expf(z - mx) : 0.0f;
+        const float sum = warp_sum(e);
+        const float ls = logf(sum), inv = 1.0f / sum;
+        if (in_vocab) lp[lane] = (z - mx) - ls;
+        if (greedy) {
+          const unsigned top = __ballot_sync(0xffffffffu, in_vocab && z == mx);
+          tok = top ? __ffs(top) - 1 : 0;
         } else {
-          const float temperature = M.temp[s];
-          const bool greedy = !(temperature > 0.0f);
-          const float T = (temperature > 0.0f && isfinite(temperature)) ? temperature : 1.0f;
-          float zz[kV], prob[kV];
-          float mx = -INFINITY;
-          for (int v = 0; v < kV; ++v) {
-            zz[v] = Lg[s][v] / T;
-            mx = fmaxf(mx, zz[v]);
-          }
-          float sum = 0.0f;
-          for (int v = 0; v < kV; ++v) {
-            prob[v] = expf(zz[v] - mx);
-            sum += prob[v];
-          }
-          const float ls = logf(sum), inv = 1.0f / sum;
-          for (int v = 0; v < kV; ++v) {
-            prob[v] *= inv;
-            lp[v] = (zz[v] - mx) - ls;
-          }
-          if (greedy) {
-            tok = 0;
-            for (int v = 1; v < kV; ++v)
-              if (zz[v] > zz[tok]) tok = v;
-          } else {
+          double u = 0.0;
+          if (lane == 0) {
             unsigned long long r = M.rng[s];
-            const double u = (double)(splitmix_next(r) >> 11) * (1.0 / 9007199254740992.0);
+            u = (double)(splitmix_next(r) >> 11) * (1.0 / 9007199254740992.0);
             M.rng[s] = r;
-            double cum = 0.0;
-            for (int v = 0; v < kV; ++v) {
-              cum += (double)prob[v];
-              if (u < cum) {
-                tok = v;
-                break;
-              }
-            }
           }
+          u = __shfl_sync(0xffffffffu, u, 0);
+          double cum = in_vocab ? (double)(e * inv) : 0.0;
+#pragma unroll
+          for (int d = 1; d < 32; d <<= 1) {
+            const double o = __shfl_up_sync(0xffffffffu, cum, d);
+            if (lane >= d) cum += o;
+          }
+          const unsigned hit = __ballot_sync(0xffffffffu, in_vocab && u < cum);
+          if (hit) tok = __ffs(hit) - 1;
         }
-        a.tokens[q] = tok;
       }
+      if (lane == 0) a.tokens[q] = tok;
     }
     __syncthreads();
   }
