@@ -22,7 +22,8 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU_SOURCES = ["kernels_f32.cu", "kernels_tc.cu", "gemm_tc.cu", "engine.cu", "noalloc.cu"]
+CU_SOURCES = ["kernels_f32.cu", "kernels_tc.cu", "gemm_tc.cu", "enc_tc.cu", "engine.cu",
+              "noalloc.cu"]
 CPP_SOURCES = ["host_order.cpp", "host_synth.cpp", "safetensors.cpp"]
 
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",

@@ -1,0 +1,500 @@
+// Fused tcgen05 encoder-layer kernels for the tensor-core modes.  h_E is kept
+// in HBM as fp16 [R*48, 128] (slot s = residue * 48 + k) and every edge-wise
+// chain of an encoder layer runs in one pass over it, so no [R*48, 128]
+// intermediate ever goes to HBM:
+//
+//   enc_node_tc  (proteinmpnn_encoder_scalar.cpp:169-243)
+//     D1 = W1b h_E                        M = 128 features, N = 192 slots
+//     G  = GELU(D1 + [W1a h_i + b1] + W1c h_j)  (node terms gathered per slot)
+//     D2 = W2 G
+//     S_i = sum_k m_i m_j GELU(D2 + b2),  cnt_i = sum_k m_i m_j
+//   Weights are the A operand and the 4 residues' 192 slots the B operand, so
+//   a residue's 48 slots are 48 TMEM columns of one thread: the neighbour sum
+//   is a thread-local loop in a fixed order (deterministic, no atomics).
+//
+//   enc_edge_tc  (proteinmpnn_encoder_scalar.cpp:289-321)
+//     D1 = h_E W11b^T                     M = 128 slots, N = 128 features
+//     G  = GELU(D1 + [W11a h_i + b11] + W11c h_j)
+//     G  = GELU(G W12^T + b12)
+//     h_E = LN3(h_E + G W13^T + b13)      on slots with a valid neighbour
+//   Slots are the A operand here (TMEM lanes), so each slot's 128 features are
+//   one TMEM row; the LayerNorm statistics combine the four 32-column parts.
+//
+// Both are persistent (one CTA per SM, 16 warps).  Weight images stay resident
+// in shared memory (bulk copies), the h_E tile of the next step is fetched by
+// cp.async into the second buffer while the current one is processed, and the
+// three (two) MMAs of a tile are issued by thread 0 and completion-tracked on
+// one mbarrier.  Every wait is bounded.
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "kernels.hpp"
+#include "tcgen05.cuh"
+
+namespace hkb {
+namespace {
+
+using namespace tc;
+
+constexpr int kEncThreads = 512;
+constexpr uint32_t kW128Bytes = 128 * 128 * 2;   // one 128x128 fp16 weight image
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool pred) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(pred ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t idesc_f16(int M, int N) {
+  return idesc_bf16(M, N) & ~((7u << 7) | (7u << 10));
+}
+
+// Copies `rows` rows of 128 fp16 (256 B) starting at global row `row0` into a
+// SW128 K-major tile of `tile_rows` rows; rows at or past `row_end` read as 0.
+__device__ __forceinline__ void load_rows_async(unsigned char* tile, const uint16_t* src,
+                                                int64_t row0, int64_t row_end, int tile_rows,
+                                                int tid) {
+  const int chunks = tile_rows * 16;
+  for (int c = tid; c < chunks; c += kEncThreads) {
+    const int r = c >> 4, k8 = c & 15;
+    const int64_t gr = row0 + r;
+    const bool ok = gr < row_end;
+    const uint16_t* p = src + (ok ? gr : 0) * kH + k8 * 8;
+    cp_async16(tile + sw128_offset(r, k8 * 8, tile_rows), p, ok);
+  }
+}
+
+__device__ __forceinline__ void load_weights(unsigned char* dst, const unsigned char* const* imgs,
+                                             int n, uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, (uint32_t)n * kW128Bytes);
+  for (int i = 0; i < n; ++i)
+    for (uint32_t o = 0; o < kW128Bytes; o += 16384u)
+      bulk_g2s(dst + (size_t)i * kW128Bytes + o, imgs[i] + o, 16384u, bar);
+}
+
+// ---------------------------------------------------------------------------
+// Node-message kernel: 4 residues (192 slots) per tile.
+// ---------------------------------------------------------------------------
+constexpr int kNodeRes = 4;
+constexpr int kNodeSlots = kNodeRes * kK;                  // 192
+constexpr uint32_t kNodeTileBytes = kNodeSlots * 256;      // 48 KiB
+constexpr uint32_t kNodeOffW = 0;                          // W1b, W2
+constexpr uint32_t kNodeOffB = 2 * kW128Bytes;             // 2 h_E tiles
+constexpr uint32_t kNodeOffG = kNodeOffB + 2 * kNodeTileBytes;
+constexpr uint32_t kNodeOffJ = kNodeOffG + kNodeTileBytes; // int [192] rj, float [192] att
+constexpr uint32_t kNodeSmem = kNodeOffJ + 2 * kNodeSlots * 4 + 1024;
+
+__global__ void __launch_bounds__(kEncThreads, 1)
+    enc_node_tc_kernel(EncNodeTcArgs p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  int* SJ = reinterpret_cast<int*>(sm + kNodeOffJ);
+  float* SA = reinterpret_cast<float*>(sm + kNodeOffJ + kNodeSlots * 4);
+  __shared__ uint64_t bar_w, bar_mma;
+  __shared__ uint32_t tmem_base;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, rho = warp >> 2;      // feature quadrant, residue of the tile
+  const int f = quad * 32 + lane;
+  const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+  const int R = p.bv.total_residues;
+  const int64_t SL = (int64_t)R * kK;
+  const int tiles = (R + kNodeRes - 1) / kNodeRes;
+
+  if (tid == 0) {
+    mbar_init(&bar_w, 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_base;
+  if (tid == 0) {
+    const unsigned char* imgs[2] = {p.W1b, p.W2};
+    load_weights(sm + kNodeOffW, imgs, 2, &bar_w);
+  }
+  bool ok = true;
+  if (!mbar_wait(&bar_w, 0, p.err)) ok = false;
+  uint32_t ph = 0;
+  const float b2 = p.b2[f];
+
+  int t = blockIdx.x;
+  if (t < tiles)
+    load_rows_async(sm + kNodeOffB, p.h_e, (int64_t)t * kNodeSlots, SL, kNodeSlots, tid);
+  cp_async_commit();
+  for (int it = 0; t < tiles; t += gridDim.x, ++it) {
+    if (__syncthreads_or(!ok)) break;
+    const int buf = it & 1;
+    unsigned char* btile = sm + kNodeOffB + buf * kNodeTileBytes;
+    cp_async_wait_all();
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      mma_k128(tm, smem_u32(sm + kNodeOffW), smem_u32(btile), kNodeSlots,
+               idesc_f16(128, kNodeSlots), false);
+      mma_commit(&bar_mma);
+    }
+    // next tile's rows (its buffer was last read by the previous tile's MMA,
+    // which completed before that tile's epilogue)
+    const int tn = t + gridDim.x;
+    if (tn < tiles)
+      load_rows_async(sm + kNodeOffB + (buf ^ 1) * kNodeTileBytes, p.h_e,
+                      (int64_t)tn * kNodeSlots, SL, kNodeSlots, tid);
+    cp_async_commit();
+    // neighbour rows and attention weights of this tile's slots
+    if (tid < kNodeSlots) {
+      const int r = t * kNodeRes + tid / kK, k = tid % kK;
+      int rj = -1;
+      float att = 0.0f;
+      if (r < R) {
+        const int b = p.bv.res_prot[r];
+        const int L = p.bv.prot_len[b];
+        const int K = L < kK ? L : kK;
+        const int j = k < K ? p.e_idx[(int64_t)r * kK + k] : -1;
+        if (j >= 0 && j < L) {
+          rj = p.bv.prot_res_off[b] + j;
+          att = p.mask[r] * p.mask[rj];
+        }
+      }
+      SJ[tid] = rj;
+      SA[tid] = att;
+    }
+    __syncthreads();
+    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+    ph ^= 1;
+    tc_fence_after();
+    // epilogue 1: G[slot][f] = GELU(D1 + N_i + N_j)  (16-bit stores, B layout)
+    const int r = t * kNodeRes + rho;
+    const float na = r < R ? p.NAC[(int64_t)r * 256 + f] : 0.0f;
+    unsigned char* G = sm + kNodeOffG;
+    {
+      float v[32];
+      tmem_ld32(tm + lane_base + (uint32_t)(rho * kK), v);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const int c = rho * kK + k;
+        const int rj = SJ[c];
+        const float nc = rj >= 0 ? p.NAC[(int64_t)rj * 256 + 128 + f] : 0.0f;
+        const float y = rj >= 0 ? gelu_as(v[k] + na + nc) : 0.0f;
+        *reinterpret_cast<__half*>(G + sw128_offset(c, f, kNodeSlots)) = __float2half_rn(y);
+      }
+    }
+    {
+      float v[16];
+      tmem_ld16(tm + lane_base + (uint32_t)(rho * kK + 32), v);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int c = rho * kK + 32 + k;
+        const int rj = SJ[c];
+        const float nc = rj >= 0 ? p.NAC[(int64_t)rj * 256 + 128 + f] : 0.0f;
+        const float y = rj >= 0 ? gelu_as(v[k] + na + nc) : 0.0f;
+        *reinterpret_cast<__half*>(G + sw128_offset(c, f, kNodeSlots)) = __float2half_rn(y);
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      mma_k128(tm, smem_u32(sm + kNodeOffW + kW128Bytes), smem_u32(G), kNodeSlots,
+               idesc_f16(128, kNodeSlots), false);
+      mma_commit(&bar_mma);
+    }
+    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+    ph ^= 1;
+    tc_fence_after();
+    // epilogue 2: masked slot sum of GELU(D2 + b2), slots in ascending order
+    {
+      float total = 0.0f, cnt = 0.0f;
+      float v[32];
+      tmem_ld32(tm + lane_base + (uint32_t)(rho * kK), v);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const float a = SA[rho * kK + k];
+        if (a != 0.0f) {
+          total += a * gelu_erf(v[k] + b2);
+          cnt += a;
+        }
+      }
+      float w[16];
+      tmem_ld16(tm + lane_base + (uint32_t)(rho * kK + 32), w);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float a = SA[rho * kK + 32 + k];
+        if (a != 0.0f) {
+          total += a * gelu_erf(w[k] + b2);
+          cnt += a;
+        }
+      }
+      if (r < R) {
+        p.S[(int64_t)r * kH + f] = total;
+        if (f == 0) p.cnt[r] = cnt;
+      }
+    }
+    tc_fence_before();
+  }
+  cp_async_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, 256);
+}
+
+// ---------------------------------------------------------------------------
+// Edge-update kernel: 128 slots per tile.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kEdgeTileBytes = 128 * 256;             // 32 KiB
+constexpr uint32_t kEdgeOffW = 0;                          // W11b, W12, W13
+constexpr uint32_t kEdgeOffA = 3 * kW128Bytes;             // 2 h_E tiles
+constexpr uint32_t kEdgeOffG = kEdgeOffA + 2 * kEdgeTileBytes;
+constexpr uint32_t kEdgeOffRed = kEdgeOffG + kEdgeTileBytes;   // float [2][4][128]
+constexpr uint32_t kEdgeSmem = kEdgeOffRed + 2 * 4 * 128 * 4 + 1024;
+
+__global__ void __launch_bounds__(kEncThreads, 1)
+    enc_edge_tc_kernel(EncEdgeTcArgs p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  float (*red)[4][128] = reinterpret_cast<float (*)[4][128]>(sm + kEdgeOffRed);
+  __shared__ uint64_t bar_w, bar_mma;
+  __shared__ uint32_t tmem_base;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, cg = warp >> 2;       // slot quadrant, 32-column group
+  const int row = quad * 32 + lane;
+  const int c0 = cg * 32;
+  const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+  const int R = p.bv.total_residues;
+  const int64_t SL = (int64_t)R * kK;
+  const int64_t tiles = (SL + 127) / 128;
+
+  if (tid == 0) {
+    mbar_init(&bar_w, 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_base;
+  if (tid == 0) {
+    const unsigned char* imgs[3] = {p.W11b, p.W12, p.W13};
+    load_weights(sm + kEdgeOffW, imgs, 3, &bar_w);
+  }
+  bool ok = true;
+  if (!mbar_wait(&bar_w, 0, p.err)) ok = false;
+  uint32_t ph = 0;
+  const uint32_t idesc = idesc_f16(128, 128);
+  unsigned char* G = sm + kEdgeOffG;
+
+  int64_t t = blockIdx.x;
+  if (t < tiles) load_rows_async(sm + kEdgeOffA, p.h_e, t * 128, SL, 128, tid);
+  cp_async_commit();
+  for (int it = 0; t < tiles; t += gridDim.x, ++it) {
+    if (__syncthreads_or(!ok)) break;
+    const int buf = it & 1;
+    unsigned char* atile = sm + kEdgeOffA + buf * kEdgeTileBytes;
+    cp_async_wait_all();
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      mma_k128(tm, smem_u32(atile), smem_u32(sm + kEdgeOffW), 128, idesc, false);
+      mma_commit(&bar_mma);
+    }
+    const int64_t tn = t + gridDim.x;
+    if (tn < tiles)
+      load_rows_async(sm + kEdgeOffA + (buf ^ 1) * kEdgeTileBytes, p.h_e, tn * 128, SL, 128, tid);
+    cp_async_commit();
+    // this thread's slot
+    const int64_t s = t * 128 + row;
+    int r = 0, rj = -1;
+    if (s < SL) {
+      r = (int)(s / kK);
+      const int k = (int)(s % kK);
+      const int b = p.bv.res_prot[r];
+      const int L = p.bv.prot_len[b];
+      const int K = L < kK ? L : kK;
+      const int j = k < K ? p.e_idx[s] : -1;
+      if (j >= 0 && j < L) rj = p.bv.prot_res_off[b] + j;
+    }
+    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+    ph ^= 1;
+    tc_fence_after();
+    // epilogue 1: G = GELU(D1 + N_i + N_j) on this thread's 32 columns
+    {
+      float v[32];
+      tmem_ld32(tm + lane_base + (uint32_t)c0, v);
+      uint32_t pk[16];
+      if (rj >= 0) {
+        const float4* na = reinterpret_cast<const float4*>(p.NAC + (int64_t)r * 256 + c0);
+        const float4* nc = reinterpret_cast<const float4*>(p.NAC + (int64_t)rj * 256 + 128 + c0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 a = na[q], c = nc[q];
+          const float y0 = gelu_as(v[4 * q + 0] + a.x + c.x);
+          const float y1 = gelu_as(v[4 * q + 1] + a.y + c.y);
+          const float y2 = gelu_as(v[4 * q + 2] + a.z + c.z);
+          const float y3 = gelu_as(v[4 * q + 3] + a.w + c.w);
+          pk[2 * q] = pack_h2(y0, y1);
+          pk[2 * q + 1] = pack_h2(y2, y3);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) pk[q] = 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(G + sw128_offset(row, c0 + 8 * u, 128)) =
+            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      mma_k128(tm + 128, smem_u32(G), smem_u32(sm + kEdgeOffW + kW128Bytes), 128, idesc, false);
+      mma_commit(&bar_mma);
+    }
+    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+    ph ^= 1;
+    tc_fence_after();
+    // epilogue 2: G = GELU(D2 + b12)   (G was consumed by the MMA above)
+    {
+      float v[32];
+      tmem_ld32(tm + lane_base + 128u + (uint32_t)c0, v);
+      uint32_t pk[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        pk[q] = pack_h2(gelu_erf(v[2 * q] + p.b12[c0 + 2 * q]),
+                        gelu_erf(v[2 * q + 1] + p.b12[c0 + 2 * q + 1]));
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(G + sw128_offset(row, c0 + 8 * u, 128)) =
+            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      mma_k128(tm, smem_u32(G), smem_u32(sm + kEdgeOffW + 2 * kW128Bytes), 128, idesc, false);
+      mma_commit(&bar_mma);
+    }
+    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+    ph ^= 1;
+    tc_fence_after();
+    // epilogue 3: x = h_E + D3 + b13, LayerNorm over the row's 128 features
+    // (four 32-column parts held by warps quad, quad+4, quad+8, quad+12)
+    {
+      float x[32];
+      tmem_ld32(tm + lane_base + (uint32_t)c0, x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint4 hv = *reinterpret_cast<const uint4*>(atile + sw128_offset(row, c0 + 8 * u, 128));
+        const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 h2 = __half22float2(*reinterpret_cast<const __half2*>(&hw[i]));
+          const int c = 8 * u + 2 * i;
+          x[c] += h2.x + p.b13[c0 + c];
+          x[c + 1] += h2.y + p.b13[c0 + c + 1];
+        }
+      }
+      float sum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sum += x[i];
+      red[0][cg][row] = sum;
+      __syncthreads();
+      const float mean =
+          (red[0][0][row] + red[0][1][row] + red[0][2][row] + red[0][3][row]) * (1.0f / 128.0f);
+      float sq = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        x[i] -= mean;
+        sq += x[i] * x[i];
+      }
+      red[1][cg][row] = sq;
+      __syncthreads();
+      const float var =
+          (red[1][0][row] + red[1][1][row] + red[1][2][row] + red[1][3][row]) * (1.0f / 128.0f);
+      const float inv = 1.0f / sqrtf(var + kLnEps);
+      if (rj >= 0) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const int c = c0 + 2 * q;
+          pk[q] = pack_h2(x[2 * q] * inv * p.n3w[c] + p.n3b[c],
+                          x[2 * q + 1] * inv * p.n3w[c + 1] + p.n3b[c + 1]);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(p.h_e_out + s * kH + c0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+      }
+    }
+    tc_fence_before();
+  }
+  cp_async_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, 256);
+}
+
+template <typename K>
+void set_smem(K kernel, uint32_t bytes) {
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+}  // namespace
+
+void launch_enc_node_tc(cudaStream_t st, const EncNodeTcArgs& p, int num_sms) {
+  const int tiles = (p.bv.total_residues + kNodeRes - 1) / kNodeRes;
+  if (tiles <= 0) return;
+  static bool attr = false;
+  if (!attr) {
+    set_smem(enc_node_tc_kernel, kNodeSmem);
+    attr = true;
+  }
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  enc_node_tc_kernel<<<grid, kEncThreads, kNodeSmem, st>>>(p);
+}
+
+void launch_enc_edge_tc(cudaStream_t st, const EncEdgeTcArgs& p, int num_sms) {
+  const int64_t tiles = ((int64_t)p.bv.total_residues * kK + 127) / 128;
+  if (tiles <= 0) return;
+  static bool attr = false;
+  if (!attr) {
+    set_smem(enc_edge_tc_kernel, kEdgeSmem);
+    attr = true;
+  }
+  const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+  enc_edge_tc_kernel<<<grid, kEncThreads, kEdgeSmem, st>>>(p);
+}
+
+}  // namespace hkb

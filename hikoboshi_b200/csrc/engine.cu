@@ -698,12 +698,11 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   eo->e_idx = ws.get_as<int>("e.idx", SL);
   eo->d2 = ws.get_as<float>("e.d2", SL);
   eo->mask = ws.get_as<float>("e.mask", R);
-  eo->h_e = ws.get_as<float>("e.he", SL * kH);
+  eo->h_e = nullptr;
+  eo->h_e16 = ws.get_as<uint16_t>("e.he16", SL * kH);
   eo->h_v = ws.get_as<float>("e.hv", R * kH);
   float* feat = ws.get_as<float>("e.feat", SL * kEdgeIn);
   float* E1 = ws.get_as<float>("e.s1", SL * kH);
-  float* EB = ws.get_as<float>("e.s2", SL * kH);
-  float* G1 = ws.get_as<float>("e.s3", SL * kH);
   float* NAC = ws.get_as<float>("e.nac", R * 256);
   float* Sv = ws.get_as<float>("e.S", R * kH);
   float* cnt = ws.get_as<float>("e.cnt", R);
@@ -711,8 +710,8 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   float* h1 = ws.get_as<float>("e.h1", R * kH);
   float* F = ws.get_as<float>("e.F", R * kFfn);
   float* Y = ws.get_as<float>("e.Y", R * kH);
-  if (!eo->e_idx || !eo->d2 || !eo->mask || !eo->h_e || !eo->h_v || !feat || !E1 ||
-      !EB || !G1 || !NAC || !Sv || !cnt || !T3 || !h1 || !F || !Y)
+  if (!eo->e_idx || !eo->d2 || !eo->mask || !eo->h_e16 || !eo->h_v || !feat || !E1 ||
+      !NAC || !Sv || !cnt || !T3 || !h1 || !F || !Y)
     return {HKB_UNAVAILABLE, "device allocation failed"};
   const BatchView& bv = db.bv;
   auto lin = [&](int64_t M, int N, int K, const void* A, int64_t lda, const char* img,
@@ -738,29 +737,50 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   e->launches += 2;
   lin(SL, kH, kEdgeIn, feat, kEdgeIn, "edge", nullptr, 0, E1, kH, false);
   launch_ln_rows(st, SL, E1, nullptr, nullptr, w.norm_e_w, w.norm_e_b, nullptr, nullptr, E1);
-  lin(SL, kH, kH, E1, kH, "W_e", w.We_b, 0, eo->h_e, kH, false);
+  lin(SL, kH, kH, E1, kH, "W_e", w.We_b, 0, eo->h_e16, kH, true);
   HKB_CUDA(cudaMemsetAsync(eo->h_v, 0, sizeof(float) * R * kH, st));
   e->launches += 1;
   for (int l = 0; l < 3; ++l) {
     const auto& E = w.enc[l];
     const std::string q = "enc" + std::to_string(l) + ".";
+    // node messages: one fused pass over h_E (W1b, gathers, GELU, W2, GELU, slot sum)
     lin(R, 256, kH, eo->h_v, kH, (q + "W1ac").c_str(), E.b1ac, 0, NAC, 256, false);
-    lin(SL, kH, kH, eo->h_e, kH, (q + "W1b").c_str(), nullptr, 0, EB, kH, false);
-    launch_enc_msg_in(st, bv, NAC, EB, eo->e_idx, G1);
-    lin(SL, kH, kH, G1, kH, (q + "W2").c_str(), E.b2, 1, EB, kH, false);
-    launch_enc_aggregate(st, bv, EB, eo->e_idx, eo->mask, Sv, cnt);
+    EncNodeTcArgs na;
+    na.bv = bv;
+    na.h_e = eo->h_e16;
+    na.e_idx = eo->e_idx;
+    na.mask = eo->mask;
+    na.NAC = NAC;
+    na.W1b = e->gemm_img.at(q + "W1b");
+    na.W2 = e->gemm_img.at(q + "W2");
+    na.b2 = E.b2;
+    na.S = Sv;
+    na.cnt = cnt;
+    na.err = e->d_err;
+    launch_enc_node_tc(st, na, e->num_sms);
     lin(R, kH, kH, Sv, kH, (q + "W3").c_str(), nullptr, 0, T3, kH, false);
     launch_enc_node_update(st, bv, T3, cnt, E.b3, eo->h_v, E.n1w, E.n1b, h1);
     lin(R, kFfn, kH, h1, kH, (q + "Win").c_str(), E.bin, 1, F, kFfn, false);
     lin(R, kH, kFfn, F, kFfn, (q + "Wout").c_str(), nullptr, 0, Y, kH, false);
     launch_ln_rows(st, R, h1, Y, E.bout, E.n2w, E.n2b, eo->mask, nullptr, eo->h_v);
+    // edge update: one fused pass (W11b, gathers, GELU, W12, GELU, W13, LN3)
     lin(R, 256, kH, eo->h_v, kH, (q + "W11ac").c_str(), E.b11ac, 0, NAC, 256, false);
-    lin(SL, kH, kH, eo->h_e, kH, (q + "W11b").c_str(), nullptr, 0, EB, kH, false);
-    launch_enc_msg_in(st, bv, NAC, EB, eo->e_idx, G1);
-    lin(SL, kH, kH, G1, kH, (q + "W12").c_str(), E.b12, 1, EB, kH, false);
-    lin(SL, kH, kH, EB, kH, (q + "W13").c_str(), E.b13, 0, G1, kH, false);
-    launch_edge_ln_update(st, bv, G1, eo->e_idx, E.n3w, E.n3b, eo->h_e);
-    e->launches += 6;
+    EncEdgeTcArgs ea;
+    ea.bv = bv;
+    ea.h_e = eo->h_e16;
+    ea.h_e_out = eo->h_e16;
+    ea.e_idx = eo->e_idx;
+    ea.NAC = NAC;
+    ea.W11b = e->gemm_img.at(q + "W11b");
+    ea.W12 = e->gemm_img.at(q + "W12");
+    ea.W13 = e->gemm_img.at(q + "W13");
+    ea.b12 = E.b12;
+    ea.b13 = E.b13;
+    ea.n3w = E.n3w;
+    ea.n3b = E.n3b;
+    ea.err = e->d_err;
+    launch_enc_edge_tc(st, ea, e->num_sms);
+    e->launches += 4;
   }
   HKB_CUDA(cudaGetLastError());
   return kOk;
@@ -782,9 +802,10 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const EncoderOu
     p.K = kH;
     p.err = e->d_err;
     p.out_f16 = true;
-    p.M = SL; p.A = eo.h_e; p.lda = kH; p.W = e->gemm_img.at(q + "W1b"); p.C = pe; p.ldc = kH;
+    p.M = SL; p.A = eo.h_e16; p.a_f16 = true; p.lda = kH; p.W = e->gemm_img.at(q + "W1b");
+    p.C = pe; p.ldc = kH;
     launch_linear_tc(st, p, e->num_sms);
-    p.M = R; p.A = eo.h_v; p.W = e->gemm_img.at(q + "W1d"); p.C = pv;
+    p.M = R; p.A = eo.h_v; p.a_f16 = false; p.W = e->gemm_img.at(q + "W1d"); p.C = pv;
     launch_linear_tc(st, p, e->num_sms);
     tb->PE[l] = pe;
     tb->PVenc[l] = pv;
@@ -1427,6 +1448,32 @@ static hkb_status single_protein_encode(hkb_engine* e, int32_t L, const float* c
   return kOk;
 }
 
+// IEEE binary16 -> binary32 (exact).
+static float half_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h >> 15) << 31;
+  uint32_t ex = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+  uint32_t bits;
+  if (ex == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {   // subnormal: renormalise
+      ex = 113;
+      while (!(man & 0x400u)) {
+        man <<= 1;
+        --ex;
+      }
+      bits = sign | (ex << 23) | ((man & 0x3FFu) << 13);
+    }
+  } else if (ex == 31) {
+    bits = sign | 0x7F800000u | (man << 13);
+  } else {
+    bits = sign | ((ex + 112) << 23) | (man << 13);
+  }
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+
 static void compact_rows(const void* src, void* dst, int L, int K, size_t elem, size_t width) {
   // [L,48,width] -> [L,K,width]
   for (int i = 0; i < L; ++i)
@@ -1444,13 +1491,19 @@ hkb_status hkb_mpnn_encode(hkb_engine* e, int32_t L, const float* coords,
   if (s.code != HKB_OK) return s;
   const int K = std::min(L, kK);
   std::vector<float> he((size_t)L * kK * kH);
+  std::vector<uint16_t> he16(eo.h_e16 ? he.size() : 0);
   std::vector<int> idx((size_t)L * kK);
   cudaStream_t st = e->stream;
   if (h_v) HKB_CUDA(cudaMemcpyAsync(h_v, eo.h_v, sizeof(float) * L * kH, cudaMemcpyDeviceToHost, st));
-  HKB_CUDA(cudaMemcpyAsync(he.data(), eo.h_e, he.size() * sizeof(float), cudaMemcpyDeviceToHost, st));
+  if (eo.h_e16)
+    HKB_CUDA(cudaMemcpyAsync(he16.data(), eo.h_e16, he16.size() * sizeof(uint16_t),
+                             cudaMemcpyDeviceToHost, st));
+  else
+    HKB_CUDA(cudaMemcpyAsync(he.data(), eo.h_e, he.size() * sizeof(float), cudaMemcpyDeviceToHost, st));
   HKB_CUDA(cudaMemcpyAsync(idx.data(), eo.e_idx, idx.size() * sizeof(int), cudaMemcpyDeviceToHost, st));
   s = check_device_error(e);
   if (s.code != HKB_OK) return s;
+  for (size_t i = 0; i < he16.size(); ++i) he[i] = half_to_float(he16[i]);
   if (h_e) compact_rows(he.data(), h_e, L, K, sizeof(float), kH);
   if (e_idx) compact_rows(idx.data(), e_idx, L, K, sizeof(int), 1);
   return kOk;

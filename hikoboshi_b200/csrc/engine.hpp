@@ -62,7 +62,8 @@ struct EncoderOut {
   int* e_idx = nullptr;   // [R,48]
   float* d2 = nullptr;    // [R,48]
   float* mask = nullptr;  // [R]
-  float* h_e = nullptr;   // [R,48,128]
+  float* h_e = nullptr;   // [R,48,128] (fp32 encoder)
+  uint16_t* h_e16 = nullptr;  // [R,48,128] fp16 (tensor-core encoder)
   float* h_v = nullptr;   // [R,128]
 };
 

@@ -225,6 +225,40 @@ struct LinearTcArgs {
 size_t linear_tc_smem_bytes(int N, int K);
 void launch_linear_tc(cudaStream_t st, const LinearTcArgs& p, int num_sms);
 
+// Fused encoder-layer kernels (tensor-core modes; h_E fp16 [R*48,128]).
+// NAC = [W1a h + b1 | W1c h] per residue, fp32 [R,256].
+struct EncNodeTcArgs {
+  BatchView bv;
+  const uint16_t* h_e = nullptr;
+  const int* e_idx = nullptr;
+  const float* mask = nullptr;
+  const float* NAC = nullptr;
+  const unsigned char* W1b = nullptr;   // fp16 SW128 images [128 out x 128 in]
+  const unsigned char* W2 = nullptr;
+  const float* b2 = nullptr;
+  float* S = nullptr;                   // [R,128] masked slot sums of GELU(W2 g + b2)
+  float* cnt = nullptr;                 // [R] sum of m_i m_j
+  unsigned int* err = nullptr;
+};
+void launch_enc_node_tc(cudaStream_t st, const EncNodeTcArgs& p, int num_sms);
+
+struct EncEdgeTcArgs {
+  BatchView bv;
+  const uint16_t* h_e = nullptr;        // read
+  uint16_t* h_e_out = nullptr;          // written on slots with a valid neighbour (may alias)
+  const int* e_idx = nullptr;
+  const float* NAC = nullptr;           // [W11a h + b11 | W11c h]
+  const unsigned char* W11b = nullptr;
+  const unsigned char* W12 = nullptr;
+  const unsigned char* W13 = nullptr;
+  const float* b12 = nullptr;
+  const float* b13 = nullptr;
+  const float* n3w = nullptr;
+  const float* n3b = nullptr;
+  unsigned int* err = nullptr;
+};
+void launch_enc_edge_tc(cudaStream_t st, const EncEdgeTcArgs& p, int num_sms);
+
 int ar_tc_group_size();
 // f32 -> fp16 (f16 = true) or bf16, round to nearest even.
 void convert_f32_to_16(cudaStream_t st, const float* src, uint16_t* dst, int64_t n, bool f16);
