@@ -224,31 +224,28 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
-    // epilogue 2: masked slot sum of GELU(D2 + b2), slots in ascending order
+    // epilogue 2: masked slot sum of GELU(D2 + b2): four interleaved partial
+    // sums (slot k goes to k % 4) combined in a fixed order
     {
-      float total = 0.0f, cnt = 0.0f;
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cnt = 0.0f;
       float v[32];
       tmem_ld32(tm + lane_base + (uint32_t)(rho * kK), v);
 #pragma unroll
       for (int k = 0; k < 32; ++k) {
         const float a = SA[rho * kK + k];
-        if (a != 0.0f) {
-          total += a * gelu_erf(v[k] + b2);
-          cnt += a;
-        }
+        acc[k & 3] += a * gelu_erf(v[k] + b2);
+        cnt += a;
       }
       float w[16];
       tmem_ld16(tm + lane_base + (uint32_t)(rho * kK + 32), w);
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
         const float a = SA[rho * kK + 32 + k];
-        if (a != 0.0f) {
-          total += a * gelu_erf(w[k] + b2);
-          cnt += a;
-        }
+        acc[k & 3] += a * gelu_erf(w[k] + b2);
+        cnt += a;
       }
       if (r < R) {
-        p.S[(int64_t)r * kH + f] = total;
+        p.S[(int64_t)r * kH + f] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
         if (f == 0) p.cnt[r] = cnt;
       }
     }

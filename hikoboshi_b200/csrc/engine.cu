@@ -524,20 +524,27 @@ hkb_status build_host_batch(int B, const int32_t* L, const int32_t* S,
 }
 
 // Decoding orders for every sequence, on host threads.
-hkb_status build_orders(const int32_t* modes, const uint64_t* seeds,
-                        const int32_t* input_orders, HostBatch* hb) {
-  hb->orders.assign(hb->Q, 0);
-  for (int b = 0; b < hb->B; ++b) {
+// Order-mode and input-permutation checks (decode_order_scalar.cpp:68-82),
+// done before any device work is queued.
+hkb_status validate_orders(const int32_t* modes, const int32_t* input_orders,
+                           const HostBatch& hb) {
+  for (int b = 0; b < hb.B; ++b) {
     const int mode = modes ? modes[b] : HKB_DECODE_RANDOM;
     if (mode == HKB_DECODE_INPUT) {
       if (input_orders == nullptr)
         return invalid("ProteinMPNN input decoding_order must be a permutation");
-      if (!check_permutation(input_orders + hb->off[b], hb->L[b]))
+      if (!check_permutation(input_orders + hb.off[b], hb.L[b]))
         return invalid("ProteinMPNN input decoding_order must be a permutation");
     } else if (mode != HKB_DECODE_RANDOM && mode != HKB_DECODE_N_TO_C) {
       return invalid("unknown decode order mode");
     }
   }
+  return kOk;
+}
+
+// Per-sequence decoding orders of a validated batch (host threads).
+void generate_orders(const int32_t* modes, const int32_t* input_orders, HostBatch* hb) {
+  hb->orders.assign(hb->Q, 0);
   const int NS = hb->NS;
   auto work = [&](int lo, int hi) {
     for (int sq = lo; sq < hi; ++sq) {
@@ -570,6 +577,12 @@ hkb_status build_orders(const int32_t* modes, const uint64_t* seeds,
     }
     for (auto& x : th) x.join();
   }
+}
+
+hkb_status build_orders(const int32_t* modes, const int32_t* input_orders, HostBatch* hb) {
+  hkb_status s = validate_orders(modes, input_orders, *hb);
+  if (s.code != HKB_OK) return s;
+  generate_orders(modes, input_orders, hb);
   return kOk;
 }
 
@@ -930,7 +943,6 @@ hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
                            cudaMemcpyHostToDevice, st));
   HKB_CUDA(cudaMemcpyAsync(temps, hb.seq_temp.data(), sizeof(float) * hb.NS,
                            cudaMemcpyHostToDevice, st));
-  HKB_CUDA(cudaMemsetAsync(PV, 0, sizeof(uint16_t) * 2 * hb.Q * kH, st));
   ArBf16Args a{};
   a.group_seq0 = d_g0;
   a.group_count = d_gc;
@@ -983,8 +995,7 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
       hb->seq_seed[sq] = (batch->seeds ? batch->seeds[b] : 0ull) + (uint64_t)q;
       hb->seq_temp[sq] = batch->temperatures ? batch->temperatures[b] : 0.1f;
     }
-  s = build_orders(batch->decode_orders, batch->seeds ? hb->seq_seed.data() : hb->seq_seed.data(),
-                   batch->input_orders, hb);
+  s = validate_orders(batch->decode_orders, batch->input_orders, *hb);
   if (s.code != HKB_OK) return s;
   e->launches = 0;
   cudaStream_t st = e->stream;
@@ -994,8 +1005,6 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
   db.sources = d_src;
   s = upload_tables(e, *hb, &db);
   if (s.code != HKB_OK) return s;
-  HKB_CUDA(cudaMemcpyAsync(out.orders, hb->orders.data(), sizeof(int32_t) * hb->Q,
-                           cudaMemcpyHostToDevice, st));
   HKB_CUDA(cudaEventRecord(e->ev[0], st));
   EncoderOut eo;
   // fp32: SIMT parity pipeline; bf16: fp32 encoder, tables rounded to bf16;
@@ -1014,6 +1023,29 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
       s = decoder_tables_bf16(e, *hb, eo, dt, &tb);
   }
   if (s.code != HKB_OK) return s;
+  // The decoding orders are only needed by the decode loop: generate them on
+  // the host while the encoder and tables run on the device.
+  generate_orders(batch->decode_orders, batch->input_orders, hb);
+  if (e->h_orders_cap < (size_t)hb->Q) {
+    if (e->h_orders) {
+      HKB_CUDA(cudaEventSynchronize(e->ev_orders));
+      cudaFreeHost(e->h_orders);
+      e->h_orders = nullptr;
+      e->h_orders_cap = 0;
+    }
+    if (cudaMallocHost(&e->h_orders, sizeof(int32_t) * hb->Q) != cudaSuccess) {
+      cudaGetLastError();
+      e->h_orders = nullptr;
+      return {HKB_UNAVAILABLE, "host allocation failed"};
+    }
+    e->h_orders_cap = hb->Q;
+  } else {
+    HKB_CUDA(cudaEventSynchronize(e->ev_orders));   // previous upload done
+  }
+  std::memcpy(e->h_orders, hb->orders.data(), sizeof(int32_t) * hb->Q);
+  HKB_CUDA(cudaMemcpyAsync(out.orders, e->h_orders, sizeof(int32_t) * hb->Q,
+                           cudaMemcpyHostToDevice, st));
+  HKB_CUDA(cudaEventRecord(e->ev_orders, st));
   HKB_CUDA(cudaEventRecord(e->ev[2], st));
   s = e->precision == HKB_PRECISION_FP32 ? decode_f32(e, *hb, db, eo, dt, out)
                                           : decode_tc(e, *hb, db, eo, tb, out);
@@ -1075,6 +1107,8 @@ hkb_status hkb_mpnn_create(const void* st_blob, size_t length, int device,
   }
   e->weights_bytes = P.blob.data.size() * sizeof(float);
   for (auto& ev : e->ev) cudaEventCreate(&ev);
+  cudaEventCreateWithFlags(&e->ev_orders, cudaEventDisableTiming);
+  cudaEventRecord(e->ev_orders, e->stream);
   if (cudaMemcpy(e->d_weights, P.blob.data.data(), e->weights_bytes,
                  cudaMemcpyHostToDevice) != cudaSuccess) {
     cudaGetLastError();
@@ -1146,6 +1180,8 @@ void hkb_mpnn_destroy(hkb_engine* e) {
   if (e->d_err) cudaFree(e->d_err);
   for (auto& ev : e->ev)
     if (ev) cudaEventDestroy(ev);
+  if (e->ev_orders) cudaEventDestroy(e->ev_orders);
+  if (e->h_orders) cudaFreeHost(e->h_orders);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -1279,7 +1315,7 @@ hkb_status hkb_mpnn_score(hkb_engine* e, const hkb_score_batch* batch, hkb_score
       if (!check_permutation(hb.orders.data() + hb.seq_row_off[sq], hb.L[hb.seq_prot[sq]]))
         return invalid("ProteinMPNN decoding_order must be a permutation");
   } else {
-    s = build_orders(nullptr, hb.seq_seed.data(), nullptr, &hb);
+    s = build_orders(nullptr, nullptr, &hb);
     if (s.code != HKB_OK) return s;
   }
   e->launches = 0;

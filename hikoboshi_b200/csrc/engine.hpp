@@ -86,4 +86,9 @@ struct hkb_engine {
   int64_t launches = 0;
   float timings[4] = {0, 0, 0, 0};
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  // pinned staging of the host-generated decoding orders; ev_orders marks the
+  // last upload from it, so the next call does not overwrite it in flight
+  int32_t* h_orders = nullptr;
+  size_t h_orders_cap = 0;
+  cudaEvent_t ev_orders = nullptr;
 };

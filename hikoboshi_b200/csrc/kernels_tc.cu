@@ -98,16 +98,17 @@ __device__ __forceinline__ float tanh_approx(float x) {
 // GELU(x) ~= x/2 (1 + tanh(u(x))) with u an odd degree-5 polynomial fitted to
 // the exact erf form: max error 2.5e-5 with exact tanh, against 4.7e-4 for
 // the textbook cubic u, whose error is one-signed over wide ranges and so
-// accumulates through the 48-slot sums.  x is clamped to [-5, 5] inside u
-// (tanh(u) has saturated there).  tanh is the hardware tanh.approx.f32.  The
-// fp32 parity path uses the reference's erf form instead.
-__device__ __forceinline__ float gelu_tc(float x) {
-  const float hx = 0.5f * x;
-  const float xc = fminf(fmaxf(x, -5.0f), 5.0f);
-  const float x2 = xc * xc;
-  const float u = xc * fmaf(fmaf(-3.51516790e-04f, x2, 3.70056460e-02f), x2, 7.97507884e-01f);
-  return fmaf(hx, tanh_approx(u), hx);
+// accumulates through the 48-slot sums.  x^2 is clamped to 25 inside the
+// polynomial: for |x| > 5 that gives |u| >= 1.50 |x| > 7.5, where tanh has
+// saturated.  tanh is the hardware tanh.approx.f32.  gelu2_tc returns twice
+// the value (x (1 + tanh u)), for sums that halve once at the end.  The fp32
+// parity path uses the reference's erf form instead.
+__device__ __forceinline__ float gelu2_tc(float x) {
+  const float x2 = fminf(x * x, 25.0f);
+  const float u = x * fmaf(fmaf(-3.51516790e-04f, x2, 3.70056460e-02f), x2, 7.97507884e-01f);
+  return fmaf(x, tanh_approx(u), x);
 }
+__device__ __forceinline__ float gelu_tc(float x) { return 0.5f * gelu2_tc(x); }
 
 template <bool F16>
 __device__ __forceinline__ uint32_t pack16(float a, float b) {
@@ -134,6 +135,23 @@ __device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
       f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
     }
   }
+}
+
+// Element-wise a + b + c of eight fp16 values, in half2 pairs.
+template <bool F16>
+__device__ __forceinline__ uint4 add3_16(const uint4 a, const uint4 b, const uint4 c) {
+  static_assert(F16, "fp16 only");
+  const uint32_t x[4] = {a.x, a.y, a.z, a.w}, y[4] = {b.x, b.y, b.z, b.w},
+                 z[4] = {c.x, c.y, c.z, c.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 r = __hadd2(__hadd2(*reinterpret_cast<const __half2*>(&x[i]),
+                                      *reinterpret_cast<const __half2*>(&y[i])),
+                              *reinterpret_cast<const __half2*>(&z[i]));
+    o[i] = *reinterpret_cast<const uint32_t*>(&r);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 template <bool F16>
@@ -356,21 +374,28 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           const int code = Nb[s][k];
           const bool bw = (code >> 16) & 1;
           const int tok = code >> 17;
-          float pe[8], pv[8], st[8];
-          unpack8<F16>(pe_raw[i], pe);
-          unpack8<F16>(v_raw[i], pv);
+          const uint4 stv =
+              bw ? reinterpret_cast<const uint4*>(StabL + tok * kH)[c8] : make_uint4(0, 0, 0, 0);
+          float tsum[8];
+          if constexpr (F16) {
+            // fp16: the three table terms add in half2 pairs (one unbiased
+            // rounding more than fp32 adds), then the fp32 node term
+            unpack8<F16>(add3_16<F16>(pe_raw[i], v_raw[i], stv), tsum);
+          } else {
+            // bf16's 8-bit mantissa is too coarse for that: fp32 adds
+            float pe[8], pv[8], st[8];
+            unpack8<F16>(pe_raw[i], pe);
+            unpack8<F16>(v_raw[i], pv);
+            unpack8<F16>(stv, st);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) tsum[q] = pe[q] + pv[q] + st[q];
+          }
           const float4 a0 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2];
           const float4 a1 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2 + 1];
           const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-          if (bw) {
-            unpack8<F16>(reinterpret_cast<const uint4*>(StabL + tok * kH)[c8], st);
-          } else {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) st[q] = 0.0f;
-          }
           float y[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) y[q] = gelu_tc(av[q] + pe[q] + pv[q] + st[q]);
+          for (int q = 0; q < 8; ++q) y[q] = gelu_tc(av[q] + tsum[q]);
           outv = make_uint4(pack16<F16>(y[0], y[1]), pack16<F16>(y[2], y[3]),
                             pack16<F16>(y[4], y[5]), pack16<F16>(y[6], y[7]));
         }
@@ -400,11 +425,14 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           for (int q = 0; q < 8; ++q) Aa[s0 + q][feat] = v[q] + b1;
         } else {
           tmem_ld8(tm + lane_base + kColPV + s0, v);
+          // Every decoded row is stored (the operand row of a masked residue
+          // is zero, so its node term is exactly 0, as the reference's zeroed
+          // hidden state gives): PV needs no initialisation.
           uint16_t* PV = a.PV + (int64_t)(l - 1) * a.total_rows * kH;
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             const int s = s0 + q;
-            if (s < n && M.m[s] != 0.0f) PV[(M.qrow[s] + M.t[s]) * kH + feat] = to16<F16>(v[q]);
+            if (s < n) PV[(M.qrow[s] + M.t[s]) * kH + feat] = to16<F16>(v[q]);
           }
         }
         tc_fence_before();
@@ -456,21 +484,24 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           ++buf_use[bf];
           tc_fence_after();
           const int s = c * kChunkSeqs + sub;
-          float total = 0.0f;
+          // four interleaved partial sums (a 48-long dependent add chain
+          // would dominate), combined in a fixed order
+          float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
           {
             float v[32];
             tmem_ld32(tm + lane_base + kColD2 + bf * kChunkN + sub * kK, v);
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (i < K) total += gelu_tc(v[i] + b2);
+              if (i < K) acc[i & 3] += gelu2_tc(v[i] + b2);
           }
           {
             float v[16];
             tmem_ld16(tm + lane_base + kColD2 + bf * kChunkN + sub * kK + 32, v);
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-              if (i + 32 < K) total += gelu_tc(v[i] + b2);
+              if (i + 32 < K) acc[i & 3] += gelu2_tc(v[i] + b2);
           }
+          const float total = 0.5f * ((acc[0] + acc[1]) + (acc[2] + acc[3]));
           if (s < n)
             *reinterpret_cast<uint16_t*>(sm + kOffSb + sw128_offset(s, feat, kGB)) =
                 to16<F16>(total);
