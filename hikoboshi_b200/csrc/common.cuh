@@ -56,6 +56,37 @@ __device__ __forceinline__ float exp_neg(float x) {
   return __fmul_rn(c_exp_neg_table[n], p);
 }
 
+// The 25 (query atom, neighbour atom) slot pairs of the RBF block, in the
+// reference's order (atom_pair_distance_scalar.cpp:21-72); slot order N=0
+// CA=1 C=2 O=3 CB=4.
+static __constant__ unsigned char c_pairs[25][2] = {
+    {1, 1}, {0, 0}, {2, 2}, {3, 3}, {4, 4}, {1, 0}, {1, 2}, {1, 3}, {1, 4},
+    {0, 2}, {0, 3}, {0, 4}, {4, 2}, {4, 3}, {3, 2}, {0, 1}, {2, 1}, {3, 1},
+    {4, 1}, {2, 0}, {3, 0}, {4, 0}, {2, 4}, {3, 4}, {2, 3}};
+
+// sqrt(|x_j - x_i|^2 + 1e-6) with the reference's operation order
+// (atom_pair_distance_scalar.cpp:122-164), every step correctly rounded.
+__device__ __forceinline__ float pair_distance(const float* xi, const float* xj) {
+  float sq = 0.0f;
+#pragma unroll
+  for (int x = 0; x < 3; ++x) {
+    const float dl = __fsub_rn(xj[x], xi[x]);
+    sq = __fadd_rn(sq, __fmul_rn(dl, dl));
+  }
+  return __fsqrt_rn(__fadd_rn(sq, 1.0e-6f));
+}
+
+// RBF f of 16 on centres linspace(2, 22), sigma = 20 / (16 / sqrt(1/2))
+// (rbf_scalar.cpp:10-35, edge_rbf_features_scalar.cpp:135-137).
+__device__ __forceinline__ float rbf_value(float dist, int f) {
+  const float sigma = (22.0f - 2.0f) / (16.0f / 0.7071067811865475f);
+  const float two_s2 = 2.0f * sigma * sigma;
+  const float step = (22.0f - 2.0f) / 15.0f;
+  const float c = __fadd_rn(2.0f, __fmul_rn((float)f, step));
+  const float dl = __fsub_rn(dist, c);
+  return exp_neg(__fdiv_rn(-__fmul_rn(dl, dl), two_s2));
+}
+
 // GELU(x) = x/2 (1 + erf(x / sqrt 2)), erf by Abramowitz & Stegun 7.1.26
 // with exp(-v^2) from exp_neg (reference: cpp/include/hikoboshi/primitives/
 // compute/gelu.hpp:22-51).  Used by the fp32 parity path.

@@ -20,7 +20,9 @@
 //   Slots are the A operand here (TMEM lanes), so each slot's 128 features are
 //   one TMEM row; the LayerNorm statistics combine the four 32-column parts.
 //
-// Both are persistent (one CTA per SM, 16 warps).  Weight images stay resident
+//   enc_featurize_tc: edge features -> W_edge -> LN -> W_e, described below.
+//
+// All are persistent (one CTA per SM, 16 warps).  Weight images stay resident
 // in shared memory (bulk copies), the h_E tile of the next step is fetched by
 // cp.async into the second buffer while the current one is processed, and the
 // three (two) MMAs of a tile are issued by thread 0 and completion-tracked on
@@ -184,28 +186,18 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
-    // epilogue 1: G[slot][f] = GELU(D1 + N_i + N_j)  (16-bit stores, B layout)
+    // epilogue 1: G[slot][f] = GELU(D1 + N_i + N_j)  (16-bit stores, B layout),
+    // 16 TMEM columns at a time
     const int r = t * kNodeRes + rho;
     const float na = r < R ? p.NAC[(int64_t)r * 256 + f] : 0.0f;
     unsigned char* G = sm + kNodeOffG;
-    {
-      float v[32];
-      tmem_ld32(tm + lane_base + (uint32_t)(rho * kK), v);
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const int c = rho * kK + k;
-        const int rj = SJ[c];
-        const float nc = rj >= 0 ? p.NAC[(int64_t)rj * 256 + 128 + f] : 0.0f;
-        const float y = rj >= 0 ? gelu_as(v[k] + na + nc) : 0.0f;
-        *reinterpret_cast<__half*>(G + sw128_offset(c, f, kNodeSlots)) = __float2half_rn(y);
-      }
-    }
-    {
+#pragma unroll 1
+    for (int k0 = 0; k0 < kK; k0 += 16) {
       float v[16];
-      tmem_ld16(tm + lane_base + (uint32_t)(rho * kK + 32), v);
+      tmem_ld16(tm + lane_base + (uint32_t)(rho * kK + k0), v);
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
-        const int c = rho * kK + 32 + k;
+        const int c = rho * kK + k0 + k;
         const int rj = SJ[c];
         const float nc = rj >= 0 ? p.NAC[(int64_t)rj * 256 + 128 + f] : 0.0f;
         const float y = rj >= 0 ? gelu_as(v[k] + na + nc) : 0.0f;
@@ -228,21 +220,16 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     // sums (slot k goes to k % 4) combined in a fixed order
     {
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cnt = 0.0f;
-      float v[32];
-      tmem_ld32(tm + lane_base + (uint32_t)(rho * kK), v);
+#pragma unroll 1
+      for (int k0 = 0; k0 < kK; k0 += 16) {
+        float v[16];
+        tmem_ld16(tm + lane_base + (uint32_t)(rho * kK + k0), v);
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const float a = SA[rho * kK + k];
-        acc[k & 3] += a * gelu_erf(v[k] + b2);
-        cnt += a;
-      }
-      float w[16];
-      tmem_ld16(tm + lane_base + (uint32_t)(rho * kK + 32), w);
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const float a = SA[rho * kK + 32 + k];
-        acc[k & 3] += a * gelu_erf(w[k] + b2);
-        cnt += a;
+        for (int k = 0; k < 16; ++k) {
+          const float a = SA[rho * kK + k0 + k];
+          acc[k & 3] += a * gelu_erf(v[k] + b2);
+          cnt += a;
+        }
       }
       if (r < R) {
         p.S[(int64_t)r * kH + f] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
@@ -463,6 +450,242 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   if (warp == 0) tmem_dealloc(tm, 256);
 }
 
+// ---------------------------------------------------------------------------
+// Featurisation kernel: 128 slots per tile (inverse_fold_scalar.cpp:236-279,
+// edge_rbf_features_scalar.cpp:45-137):
+//   f   = [W_pos[:, class(i - j)] + b_pos (16) | RBF of 25 atom pairs (400) | 0 (32)]
+//   E   = f W_edge^T          K = 448 as two chunks of 4 and 3 64-column atoms
+//   h_E = LN_e(E) W_e^T + b_e   (fp16 out)
+// Features are computed straight into the SW128 operand (fp16), so the
+// [R*48, 416] feature matrix never exists in HBM.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kAtomBytes = 128 * 128;                    // 128 rows x 64 fp16
+constexpr uint32_t kFeatOffWedge = 0;                         // 7 atoms
+constexpr uint32_t kFeatOffWe = 7 * kAtomBytes;               // 2 atoms
+constexpr uint32_t kFeatOffA = kFeatOffWe + kW128Bytes;       // 4 atoms: features / LN operand
+constexpr uint32_t kFeatOffRow = kFeatOffA + 4 * kAtomBytes;  // int [3][128]
+constexpr uint32_t kFeatOffRed = kFeatOffRow + 3 * 128 * 4;   // float [2][4][128]
+constexpr uint32_t kFeatSmem = kFeatOffRed + 2 * 4 * 128 * 4 + 1024;
+
+// One RBF item: the 16 values of atom pair p for tile row `row`, as two
+// 16-byte chunks at local column `col` of the feature chunk.
+__device__ __forceinline__ void feat_pair_item(unsigned char* A, int row, int p, int col,
+                                               const int* SR, const int* SJ,
+                                               const EncFeatTcArgs& a) {
+  uint32_t pk[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const int r = SR[row], rj = SJ[row];
+  if (rj >= 0) {
+    const int ai = c_pairs[p][0], aj = c_pairs[p][1];
+    if (a.src[(int64_t)r * 5 + ai] && a.src[(int64_t)rj * 5 + aj]) {
+      const float dist =
+          pair_distance(a.coords + ((int64_t)r * 5 + ai) * 3, a.coords + ((int64_t)rj * 5 + aj) * 3);
+#pragma unroll
+      for (int f = 0; f < 8; ++f) pk[f] = pack_h2(rbf_value(dist, 2 * f), rbf_value(dist, 2 * f + 1));
+    }
+  }
+  *reinterpret_cast<uint4*>(A + sw128_offset(row, col, 128)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  *reinterpret_cast<uint4*>(A + sw128_offset(row, col + 8, 128)) =
+      make_uint4(pk[4], pk[5], pk[6], pk[7]);
+}
+
+__global__ void __launch_bounds__(kEncThreads, 1)
+    enc_featurize_tc_kernel(EncFeatTcArgs p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  int* SR = reinterpret_cast<int*>(sm + kFeatOffRow);    // residue of the row (-1: none)
+  int* SJ = SR + 128;                                    // neighbour residue (-1: invalid)
+  int* SC = SR + 256;                                    // positional class (-1: none)
+  float (*red)[4][128] = reinterpret_cast<float (*)[4][128]>(sm + kFeatOffRed);
+  unsigned char* A = sm + kFeatOffA;
+  __shared__ uint64_t bar_w, bar_mma;
+  __shared__ uint32_t tmem_base;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, cg = warp >> 2;
+  const int row = quad * 32 + lane;
+  const int c0 = cg * 32;
+  const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+  const int R = p.bv.total_residues;
+  const int64_t SL = (int64_t)R * kK;
+  const int64_t tiles = (SL + 127) / 128;
+
+  if (tid == 0) {
+    mbar_init(&bar_w, 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_base;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar_w, 7 * kAtomBytes + kW128Bytes);
+    for (uint32_t o = 0; o < 7 * kAtomBytes; o += 16384u)
+      bulk_g2s(sm + kFeatOffWedge + o, p.Wedge + o, 16384u, &bar_w);
+    for (uint32_t o = 0; o < kW128Bytes; o += 16384u)
+      bulk_g2s(sm + kFeatOffWe + o, p.We + o, 16384u, &bar_w);
+  }
+  bool ok = true;
+  if (!mbar_wait(&bar_w, 0, p.err)) ok = false;
+  uint32_t ph = 0;
+  const uint32_t idesc = idesc_f16(128, 128);
+
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    if (__syncthreads_or(!ok)) break;
+    if (tid < 128) {
+      const int64_t s = t * 128 + tid;
+      int r = -1, rj = -1, cls = -1;
+      if (s < SL) {
+        r = (int)(s / kK);
+        const int k = (int)(s % kK);
+        const int b = p.bv.res_prot[r];
+        const int off = p.bv.prot_res_off[b];
+        const int L = p.bv.prot_len[b];
+        const int K = L < kK ? L : kK;
+        const int j = k < K ? p.e_idx[s] : -1;
+        if (j >= 0 && j < L) {
+          rj = off + j;
+          int o = (r - off) - j;
+          o = o < -32 ? -32 : (o > 32 ? 32 : o);
+          cls = o + 32;
+        }
+      }
+      SR[tid] = r;
+      SJ[tid] = rj;
+      SC[tid] = cls;
+    }
+    __syncthreads();
+    // chunk 1: positional block (columns 0-15) and pairs 0-14 (16-255)
+    for (int m = tid; m < 256 + 15 * 128; m += kEncThreads) {
+      if (m < 256) {
+        const int rw = m >> 1, h = (m & 1) * 8;
+        const int cls = SC[rw];
+        uint32_t pk[4] = {0, 0, 0, 0};
+        if (cls >= 0) {
+#pragma unroll
+          for (int d = 0; d < 4; ++d) {
+            const int d0 = h + 2 * d;
+            pk[d] = pack_h2(p.pos_w[d0 * kPosClasses + cls] + p.pos_b[d0],
+                            p.pos_w[(d0 + 1) * kPosClasses + cls] + p.pos_b[d0 + 1]);
+          }
+        }
+        *reinterpret_cast<uint4*>(A + sw128_offset(rw, h, 128)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      } else {
+        const int q = m - 256, rw = q & 127, pr = q >> 7;
+        feat_pair_item(A, rw, pr, 16 + 16 * pr, SR, SJ, p);
+      }
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      for (int kk = 0; kk < 16; ++kk) {
+        const uint32_t o = (uint32_t)(kk >> 2) * kAtomBytes + (uint32_t)(kk & 3) * 32u;
+        mma_bf16(tm, sw128_desc(smem_u32(A) + o), sw128_desc(smem_u32(sm + kFeatOffWedge) + o),
+                 idesc, kk > 0 ? 1u : 0u);
+      }
+      mma_commit(&bar_mma);
+    }
+    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+    ph ^= 1;
+    tc_fence_after();
+    // chunk 2: pairs 15-24 (columns 256-415) and zero padding (416-447)
+    for (int m = tid; m < 10 * 128 + 4 * 128; m += kEncThreads) {
+      if (m < 10 * 128) {
+        const int rw = m & 127, pr = 15 + (m >> 7);
+        feat_pair_item(A, rw, pr, 16 + 16 * pr - 256, SR, SJ, p);
+      } else {
+        const int q = m - 10 * 128, rw = q >> 2, u = q & 3;
+        *reinterpret_cast<uint4*>(A + sw128_offset(rw, 160 + 8 * u, 128)) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      for (int kk = 0; kk < 12; ++kk) {
+        const uint32_t o = (uint32_t)(kk >> 2) * kAtomBytes + (uint32_t)(kk & 3) * 32u;
+        mma_bf16(tm, sw128_desc(smem_u32(A) + o),
+                 sw128_desc(smem_u32(sm + kFeatOffWedge) + 4 * kAtomBytes + o), idesc, 1u);
+      }
+      mma_commit(&bar_mma);
+    }
+    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+    ph ^= 1;
+    tc_fence_after();
+    // LayerNorm of the 128-wide edge row (four 32-column parts) -> fp16 operand
+    {
+      float x[32];
+      tmem_ld32(tm + lane_base + (uint32_t)c0, x);
+      float sum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sum += x[i];
+      red[0][cg][row] = sum;
+      __syncthreads();
+      const float mean =
+          (red[0][0][row] + red[0][1][row] + red[0][2][row] + red[0][3][row]) * (1.0f / 128.0f);
+      float sq = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        x[i] -= mean;
+        sq += x[i] * x[i];
+      }
+      red[1][cg][row] = sq;
+      __syncthreads();
+      const float var =
+          (red[1][0][row] + red[1][1][row] + red[1][2][row] + red[1][3][row]) * (1.0f / 128.0f);
+      const float inv = 1.0f / sqrtf(var + kLnEps);
+      uint32_t pk[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int c = c0 + 2 * q;
+        pk[q] = pack_h2(x[2 * q] * inv * p.ln_w[c] + p.ln_b[c],
+                        x[2 * q + 1] * inv * p.ln_w[c + 1] + p.ln_b[c + 1]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(A + sw128_offset(row, c0 + 8 * u, 128)) =
+            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      mma_k128(tm + 128, smem_u32(A), smem_u32(sm + kFeatOffWe), 128, idesc, false);
+      mma_commit(&bar_mma);
+    }
+    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+    ph ^= 1;
+    tc_fence_after();
+    {
+      const int64_t s = t * 128 + row;
+      float v[32];
+      tmem_ld32(tm + lane_base + 128u + (uint32_t)c0, v);
+      if (s < SL) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          pk[q] = pack_h2(v[2 * q] + p.We_b[c0 + 2 * q], v[2 * q + 1] + p.We_b[c0 + 2 * q + 1]);
+        uint4* dst = reinterpret_cast<uint4*>(p.h_e + s * kH + c0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+      }
+    }
+    tc_fence_before();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, 256);
+}
+
 template <typename K>
 void set_smem(K kernel, uint32_t bytes) {
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
@@ -480,6 +703,18 @@ void launch_enc_node_tc(cudaStream_t st, const EncNodeTcArgs& p, int num_sms) {
   }
   const int grid = tiles < num_sms ? tiles : num_sms;
   enc_node_tc_kernel<<<grid, kEncThreads, kNodeSmem, st>>>(p);
+}
+
+void launch_enc_featurize_tc(cudaStream_t st, const EncFeatTcArgs& p, int num_sms) {
+  const int64_t tiles = ((int64_t)p.bv.total_residues * kK + 127) / 128;
+  if (tiles <= 0) return;
+  static bool attr = false;
+  if (!attr) {
+    set_smem(enc_featurize_tc_kernel, kFeatSmem);
+    attr = true;
+  }
+  const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+  enc_featurize_tc_kernel<<<grid, kEncThreads, kFeatSmem, st>>>(p);
 }
 
 void launch_enc_edge_tc(cudaStream_t st, const EncEdgeTcArgs& p, int num_sms) {

@@ -714,8 +714,6 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   eo->h_e = nullptr;
   eo->h_e16 = ws.get_as<uint16_t>("e.he16", SL * kH);
   eo->h_v = ws.get_as<float>("e.hv", R * kH);
-  float* feat = ws.get_as<float>("e.feat", SL * kEdgeIn);
-  float* E1 = ws.get_as<float>("e.s1", SL * kH);
   float* NAC = ws.get_as<float>("e.nac", R * 256);
   float* Sv = ws.get_as<float>("e.S", R * kH);
   float* cnt = ws.get_as<float>("e.cnt", R);
@@ -723,8 +721,8 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   float* h1 = ws.get_as<float>("e.h1", R * kH);
   float* F = ws.get_as<float>("e.F", R * kFfn);
   float* Y = ws.get_as<float>("e.Y", R * kH);
-  if (!eo->e_idx || !eo->d2 || !eo->mask || !eo->h_e16 || !eo->h_v || !feat || !E1 ||
-      !NAC || !Sv || !cnt || !T3 || !h1 || !F || !Y)
+  if (!eo->e_idx || !eo->d2 || !eo->mask || !eo->h_e16 || !eo->h_v || !NAC || !Sv || !cnt ||
+      !T3 || !h1 || !F || !Y)
     return {HKB_UNAVAILABLE, "device allocation failed"};
   const BatchView& bv = db.bv;
   auto lin = [&](int64_t M, int N, int K, const void* A, int64_t lda, const char* img,
@@ -746,11 +744,22 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
     e->launches += 1;
   };
   launch_knn(st, bv, db.coords, db.sources, eo->e_idx, eo->d2, eo->mask, e->d_err, hb.max_len);
-  launch_edge_features(st, bv, w, db.coords, db.sources, eo->e_idx, feat);
+  EncFeatTcArgs fa;
+  fa.bv = bv;
+  fa.coords = db.coords;
+  fa.src = db.sources;
+  fa.e_idx = eo->e_idx;
+  fa.pos_w = w.pos_w;
+  fa.pos_b = w.pos_b;
+  fa.Wedge = e->gemm_img.at("edge");
+  fa.We = e->gemm_img.at("W_e");
+  fa.ln_w = w.norm_e_w;
+  fa.ln_b = w.norm_e_b;
+  fa.We_b = w.We_b;
+  fa.h_e = eo->h_e16;
+  fa.err = e->d_err;
+  launch_enc_featurize_tc(st, fa, e->num_sms);
   e->launches += 2;
-  lin(SL, kH, kEdgeIn, feat, kEdgeIn, "edge", nullptr, 0, E1, kH, false);
-  launch_ln_rows(st, SL, E1, nullptr, nullptr, w.norm_e_w, w.norm_e_b, nullptr, nullptr, E1);
-  lin(SL, kH, kH, E1, kH, "W_e", w.We_b, 0, eo->h_e16, kH, true);
   HKB_CUDA(cudaMemsetAsync(eo->h_v, 0, sizeof(float) * R * kH, st));
   e->launches += 1;
   for (int l = 0; l < 3; ++l) {

@@ -259,6 +259,25 @@ struct EncEdgeTcArgs {
 };
 void launch_enc_edge_tc(cudaStream_t st, const EncEdgeTcArgs& p, int num_sms);
 
+// Edge featurisation fused with the 416->128 edge linear, its LayerNorm and
+// W_e: writes h_E (fp16 [R*48,128]) for every slot.
+struct EncFeatTcArgs {
+  BatchView bv;
+  const float* coords = nullptr;        // [R,5,3]
+  const uint8_t* src = nullptr;         // [R,5] atom sources (0 = missing)
+  const int* e_idx = nullptr;
+  const float* pos_w = nullptr;         // [16,66]
+  const float* pos_b = nullptr;         // [16]
+  const unsigned char* Wedge = nullptr; // fp16 SW128 image [128 x 448]
+  const unsigned char* We = nullptr;    // fp16 SW128 image [128 x 128]
+  const float* ln_w = nullptr;
+  const float* ln_b = nullptr;
+  const float* We_b = nullptr;
+  uint16_t* h_e = nullptr;
+  unsigned int* err = nullptr;
+};
+void launch_enc_featurize_tc(cudaStream_t st, const EncFeatTcArgs& p, int num_sms);
+
 int ar_tc_group_size();
 // f32 -> fp16 (f16 = true) or bf16, round to nearest even.
 void convert_f32_to_16(cudaStream_t st, const float* src, uint16_t* dst, int64_t n, bool f16);

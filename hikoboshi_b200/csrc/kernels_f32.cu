@@ -189,10 +189,6 @@ __global__ void __launch_bounds__(256) knn_kernel(
 // The 25 (query atom, neighbour atom) slot pairs follow the reference's table
 // (atom_pair_distance_scalar.cpp:21-72); slot order N=0 CA=1 C=2 O=3 CB=4.
 // ---------------------------------------------------------------------------
-__constant__ unsigned char c_pairs[25][2] = {
-    {1, 1}, {0, 0}, {2, 2}, {3, 3}, {4, 4}, {1, 0}, {1, 2}, {1, 3}, {1, 4},
-    {0, 2}, {0, 3}, {0, 4}, {4, 2}, {4, 3}, {3, 2}, {0, 1}, {2, 1}, {3, 1},
-    {4, 1}, {2, 0}, {3, 0}, {4, 0}, {2, 4}, {3, 4}, {2, 3}};
 
 __global__ void __launch_bounds__(256) edge_features_kernel(
     BatchView bv, const float* __restrict__ pos_w, const float* __restrict__ pos_b,
@@ -204,9 +200,6 @@ __global__ void __launch_bounds__(256) edge_features_kernel(
   const int L = bv.prot_len[b];
   const int K = L < kK ? L : kK;
   const int i = r - off;
-  const float sigma = (22.0f - 2.0f) / (16.0f / 0.7071067811865475f);
-  const float two_s2 = 2.0f * sigma * sigma;
-  const float step = (22.0f - 2.0f) / 15.0f;
   // positional block: K*16 values; padding rows zeroed.
   for (int e = threadIdx.x; e < kK * 16; e += blockDim.x) {
     const int k = e >> 4, d = e & 15;
@@ -229,21 +222,10 @@ __global__ void __launch_bounds__(256) edge_features_kernel(
       for (int f = 0; f < 16; ++f) out[f] = 0.0f;
       continue;
     }
-    const float* xi = coords + ((int64_t)r * 5 + a) * 3;
-    const float* xj = coords + ((int64_t)(off + j) * 5 + bb) * 3;
-    float sq = 0.0f;
+    const float dist = pair_distance(coords + ((int64_t)r * 5 + a) * 3,
+                                     coords + ((int64_t)(off + j) * 5 + bb) * 3);
 #pragma unroll
-    for (int x = 0; x < 3; ++x) {
-      const float dl = __fsub_rn(xj[x], xi[x]);
-      sq = __fadd_rn(sq, __fmul_rn(dl, dl));
-    }
-    const float dist = __fsqrt_rn(__fadd_rn(sq, 1.0e-6f));
-#pragma unroll
-    for (int f = 0; f < 16; ++f) {
-      const float c = __fadd_rn(2.0f, __fmul_rn((float)f, step));
-      const float dl = __fsub_rn(dist, c);
-      out[f] = exp_neg(__fdiv_rn(-__fmul_rn(dl, dl), two_s2));
-    }
+    for (int f = 0; f < 16; ++f) out[f] = rbf_value(dist, f);
   }
 }
 
