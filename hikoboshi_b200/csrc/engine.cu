@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <numeric>
 #include <thread>
 
@@ -924,6 +925,34 @@ hkb_status decoder_tables_bf16(hkb_engine* e, const HostBatch& hb, const Encoder
   return kOk;
 }
 
+// Sequence groups of the fused decode kernel (one CTA each).  A group holds
+// sequences of proteins with the same length (the CTA walks L positions);
+// groups are listed longest protein first, and each length bucket is split
+// into near-equal groups of at most ceil(NS / SMs) sequences (capped at
+// `max_group`), so that a batch that fits one wave of CTAs fills every SM.
+// `seqs` is [groups, max_group], padded with -1.
+void build_decode_groups(const HostBatch& hb, int max_group, int num_sms,
+                         std::vector<int>* seqs, std::vector<int>* counts) {
+  std::map<int, std::vector<int>, std::greater<int>> by_len;
+  for (int sq = 0; sq < hb.NS; ++sq) by_len[hb.L[hb.seq_prot[sq]]].push_back(sq);
+  const int G = std::min(max_group, std::max(1, (hb.NS + num_sms - 1) / std::max(1, num_sms)));
+  seqs->clear();
+  counts->clear();
+  for (const auto& kv : by_len) {
+    const std::vector<int>& list = kv.second;
+    const int n = (int)list.size();
+    const int ng = (n + G - 1) / G;
+    const int base = n / ng, extra = n % ng;
+    int at = 0;
+    for (int g = 0; g < ng; ++g) {
+      const int c = base + (g < extra ? 1 : 0);
+      counts->push_back(c);
+      for (int i = 0; i < max_group; ++i) seqs->push_back(i < c ? list[at + i] : -1);
+      at += c;
+    }
+  }
+}
+
 hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
                      const EncoderOut& eo, const Bf16DecodeTables& tb,
                      const DeviceDesignOut& o) {
@@ -931,14 +960,10 @@ hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   cudaStream_t st = e->stream;
   const bool f16 = e->precision == HKB_PRECISION_F16;
   const int G = ar_tc_group_size();
-  std::vector<int> g0, gc;
-  for (int b = 0; b < hb.B; ++b)
-    for (int s = 0; s < hb.S[b]; s += G) {
-      g0.push_back(hb.seq_base[b] + s);
-      gc.push_back(std::min(G, hb.S[b] - s));
-    }
-  const int ng = (int)g0.size();
-  int* d_g0 = ws.get_as<int>("a.g0", ng);
+  std::vector<int> gseq, gc;
+  build_decode_groups(hb, G, e->num_sms, &gseq, &gc);
+  const int ng = (int)gc.size();
+  int* d_g0 = ws.get_as<int>("a.gseq", (size_t)ng * G);
   int* d_gc = ws.get_as<int>("a.gc", ng);
   int* pos = ws.get_as<int>("a.pos", hb.Q);
   uint16_t* PV = ws.get_as<uint16_t>("b.PV", 2 * hb.Q * kH);
@@ -946,14 +971,15 @@ hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   float* temps = ws.get_as<float>("a.temp", hb.NS);
   if (!d_g0 || !d_gc || !pos || !PV || !seeds || !temps)
     return {HKB_UNAVAILABLE, "device allocation failed"};
-  HKB_CUDA(cudaMemcpyAsync(d_g0, g0.data(), sizeof(int) * ng, cudaMemcpyHostToDevice, st));
+  HKB_CUDA(cudaMemcpyAsync(d_g0, gseq.data(), sizeof(int) * gseq.size(), cudaMemcpyHostToDevice,
+                           st));
   HKB_CUDA(cudaMemcpyAsync(d_gc, gc.data(), sizeof(int) * ng, cudaMemcpyHostToDevice, st));
   HKB_CUDA(cudaMemcpyAsync(seeds, hb.seq_seed.data(), sizeof(uint64_t) * hb.NS,
                            cudaMemcpyHostToDevice, st));
   HKB_CUDA(cudaMemcpyAsync(temps, hb.seq_temp.data(), sizeof(float) * hb.NS,
                            cudaMemcpyHostToDevice, st));
   ArBf16Args a{};
-  a.group_seq0 = d_g0;
+  a.group_seqs = d_g0;
   a.group_count = d_gc;
   a.num_groups = ng;
   a.orders = o.orders;

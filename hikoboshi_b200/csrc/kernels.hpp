@@ -188,14 +188,14 @@ struct Bf16DecodeTables {
 };
 
 struct ArBf16Args {
-  const int* group_seq0;
+  const int* group_seqs;     // [num_groups, 16] sequence indices (same L per group)
   const int* group_count;
   int num_groups;
   const int* orders;
   int* pos;
   int* tokens;
   float* log_probs;
-  uint16_t* PV;              // bf16 [2,Q,128] (zeroed by the caller)
+  uint16_t* PV;              // 16-bit [2,Q,128] (rows written before they are read)
   const uint64_t* seq_seed;
   const float* seq_temp;
   const float* mask;

@@ -86,6 +86,7 @@ struct Misc {
   long long qrow[kGB];
   unsigned long long rng[kGB];
   float temp[kGB];
+  int off[kGB];   // first residue row of the sequence's protein
 };
 static_assert(sizeof(Misc) <= 1024, "misc block");
 
@@ -224,10 +225,12 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
 
   const int g = blockIdx.x;
-  const int seq0 = a.group_seq0[g];
+  // A group holds up to 16 sequences of proteins that share one length L
+  // (possibly several proteins); each sequence keeps its protein's residue
+  // offset.
+  const int* gseq = a.group_seqs + (int64_t)g * kGB;
   const int n = a.group_count[g];
-  const int b = bv.seq_prot[seq0];
-  const int off = bv.prot_res_off[b];
+  const int b = bv.seq_prot[gseq[0]];
   const int L = bv.prot_len[b];
   const int K = L < kK ? L : kK;
 
@@ -243,9 +246,11 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   }
   if (tid < kGB) {
     const bool live = tid < n;
-    M.qrow[tid] = live ? bv.seq_row_off[seq0 + tid] : 0;
-    M.rng[tid] = live ? a.seq_seed[seq0 + tid] : 0ull;
-    M.temp[tid] = live ? a.seq_temp[seq0 + tid] : 1.0f;
+    const int sq = live ? gseq[tid] : 0;
+    M.qrow[tid] = live ? bv.seq_row_off[sq] : 0;
+    M.rng[tid] = live ? a.seq_seed[sq] : 0ull;
+    M.temp[tid] = live ? a.seq_temp[sq] : 1.0f;
+    M.off[tid] = live ? bv.prot_res_off[bv.seq_prot[sq]] : 0;
   }
   // Zero the small operand tiles once (rows of absent sequences stay zero).
   for (int e = tid; e < 4 * 4096 / 16; e += kThreadsB)
@@ -298,7 +303,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       if (tid < n) {
         t = a.orders[M.qrow[tid] + p];
         t = (t < 0 || t >= L) ? 0 : t;
-        m = a.mask[off + t];
+        m = a.mask[M.off[tid] + t];
       }
       M.t[tid] = t;
       M.m[tid] = m;
@@ -306,14 +311,14 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     __syncthreads();
     for (int e = tid; e < kGB * kH; e += kThreadsB) {
       const int s = e >> 7, f = e & 127;
-      hS[s][f] = s < n ? tb.h_enc[(int64_t)(off + M.t[s]) * kH + f] : 0.0f;
-      Aa[s][f] = s < n ? tb.Aenc0[(int64_t)(off + M.t[s]) * kH + f] : 0.0f;
+      hS[s][f] = s < n ? tb.h_enc[(int64_t)(M.off[s] + M.t[s]) * kH + f] : 0.0f;
+      Aa[s][f] = s < n ? tb.Aenc0[(int64_t)(M.off[s] + M.t[s]) * kH + f] : 0.0f;
     }
     for (int e = tid; e < n * kK; e += kThreadsB) {
       const int s = e / kK, k = e % kK;
       int code = 0;
       if (k < K) {
-        const int64_t rt = off + M.t[s];
+        const int64_t rt = M.off[s] + M.t[s];
         int j = a.e_idx[rt * kK + k];
         if (j < 0 || j >= L) {
           atomicOr(err, kErrBadIndex);
@@ -349,12 +354,13 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           const int code = Nb[s][k];
           const int j = code & 0xFFFF;
           const bool bw = (code >> 16) & 1;
-          const int64_t rt = off + M.t[s];
+          const int64_t rt = M.off[s] + M.t[s];
           pe_raw[i] = __ldg(reinterpret_cast<const uint4*>(PE + (rt * kK + k) * kH) + c8);
           if (bw && layer > 0)   // written by this kernel: coherent load
             v_raw[i] = reinterpret_cast<const uint4*>(PVl + (M.qrow[s] + j) * kH)[c8];
           else
-            v_raw[i] = __ldg(reinterpret_cast<const uint4*>(PVenc + (int64_t)(off + j) * kH) + c8);
+            v_raw[i] =
+                __ldg(reinterpret_cast<const uint4*>(PVenc + (int64_t)(M.off[s] + j) * kH) + c8);
         }
       }
     };
