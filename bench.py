@@ -65,59 +65,103 @@ def make_inputs(rank: int):
 
 
 class ClockSampler:
-    """nvidia-smi sampled every 200 ms during the timed region."""
+    """SM clock, power and clock-event reasons sampled every 20 ms through NVML
+    (nvidia_ml_py) during the timed region; nvidia-smi at 200 ms if NVML is
+    not importable."""
 
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40,
+               "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+        self.gpu = gpu_index            # CUDA ordinal; NVML is addressed by PCI bus id
+        self.samples: list[tuple[float, float, int]] = []   # (sm MHz, power W, reasons)
+        self.max_mhz = None
         self.proc = None
-        self.lines: list[str] = []
+        self.stop_evt = threading.Event()
+        self.thread = None
+        self.backend = None
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = None
+            try:
+                import torch
+                pr = torch.cuda.get_device_properties(self.gpu)
+                bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def poll():
+                while not self.stop_evt.is_set():
+                    try:
+                        self.samples.append((
+                            float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                            pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0, int(get_reasons(h))))
+                    except Exception:
+                        pass
+                    self.stop_evt.wait(0.02)
+
+            self.backend = "nvml"
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            pass
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.backend = "nvidia-smi"
+            self.thread = threading.Thread(target=self._read_smi, daemon=True)
             self.thread.start()
         except OSError:
             self.proc = None
 
-    def _read(self):
+    def _read_smi(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
-    def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        sm, mx, reasons, power = [], None, set(), []
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
+            f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-                power.append(float(f[3]))
+                bits = 0
+                for (n, b), v in zip(self.REASONS.items(), (f[5], f[6], f[7], f[8])):
+                    if v.lower().startswith("active"):
+                        bits |= b
+                self.samples.append((float(f[1]), float(f[3]), bits))
+                self.max_mhz = float(f[2])
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
+
+    def stop(self) -> dict:
+        if self.backend is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+        self.stop_evt.set()
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        sm = [x[0] for x in self.samples]
+        power = [x[1] for x in self.samples]
+        reasons = sorted({n for n, b in self.REASONS.items()
+                          for x in self.samples if x[2] & b})
         load = [x for x, p in zip(sm, power) if p > 200] or sm
-        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm),
-                "power_w_max": max(power) if power else None}
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(sm),
+                "power_w_max": max(power) if power else None, "source": self.backend}
 
 
 def measured_peaks():

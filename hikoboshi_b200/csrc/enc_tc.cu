@@ -686,6 +686,100 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   if (warp == 0) tmem_dealloc(tm, 256);
 }
 
+// ---------------------------------------------------------------------------
+// Decoder edge tables: PE_l = h_E W1b_l^T (l = 0..2, fp16 out) in one pass over
+// h_E -- the three decoder layers' h_E input blocks (decoder_layer_scalar.cpp:
+// 26-69 split by input block) share the A tile.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kTabOffW = 0;                            // 3 images
+constexpr uint32_t kTabOffA = 3 * kW128Bytes;               // 2 h_E tiles
+constexpr uint32_t kTabSmem = kTabOffA + 2 * kEdgeTileBytes + 1024;
+
+__global__ void __launch_bounds__(kEncThreads, 1) dec_tables_tc_kernel(DecTablesTcArgs p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  __shared__ uint64_t bar_w, bar_mma;
+  __shared__ uint32_t tmem_base;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, cg = warp >> 2;
+  const int row = quad * 32 + lane;
+  const int c0 = cg * 32;
+  const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+  const int64_t SL = p.rows;
+  const int64_t tiles = (SL + 127) / 128;
+
+  if (tid == 0) {
+    mbar_init(&bar_w, 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_base;
+  if (tid == 0) {
+    const unsigned char* imgs[3] = {p.W[0], p.W[1], p.W[2]};
+    load_weights(sm + kTabOffW, imgs, 3, &bar_w);
+  }
+  bool ok = true;
+  if (!mbar_wait(&bar_w, 0, p.err)) ok = false;
+  uint32_t ph = 0;
+  const uint32_t idesc = idesc_f16(128, 128);
+
+  int64_t t = blockIdx.x;
+  if (t < tiles) load_rows_async(sm + kTabOffA, p.h_e, t * 128, SL, 128, tid);
+  cp_async_commit();
+  for (int it = 0; t < tiles; t += gridDim.x, ++it) {
+    if (__syncthreads_or(!ok)) break;
+    const int buf = it & 1;
+    unsigned char* atile = sm + kTabOffA + buf * kEdgeTileBytes;
+    cp_async_wait_all();
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      for (int l = 0; l < 3; ++l)
+        mma_k128(tm + 128u * l, smem_u32(atile), smem_u32(sm + kTabOffW + l * kW128Bytes), 128,
+                 idesc, false);
+      mma_commit(&bar_mma);
+    }
+    // next tile into the other buffer (its MMAs completed last iteration)
+    const int64_t tn = t + gridDim.x;
+    if (tn < tiles)
+      load_rows_async(sm + kTabOffA + (buf ^ 1) * kEdgeTileBytes, p.h_e, tn * 128, SL, 128, tid);
+    cp_async_commit();
+    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+    ph ^= 1;
+    tc_fence_after();
+    const int64_t s = t * 128 + row;
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+      float v[32];
+      tmem_ld32(tm + lane_base + 128u * l + (uint32_t)c0, v);
+      if (s < SL) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) pk[q] = pack_h2(v[2 * q], v[2 * q + 1]);
+        uint4* dst = reinterpret_cast<uint4*>(p.out[l] + s * kH + c0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+      }
+    }
+    tc_fence_before();
+  }
+  cp_async_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, 512);
+}
+
 template <typename K>
 void set_smem(K kernel, uint32_t bytes) {
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
@@ -715,6 +809,18 @@ void launch_enc_featurize_tc(cudaStream_t st, const EncFeatTcArgs& p, int num_sm
   }
   const int grid = (int)(tiles < num_sms ? tiles : num_sms);
   enc_featurize_tc_kernel<<<grid, kEncThreads, kFeatSmem, st>>>(p);
+}
+
+void launch_dec_tables_tc(cudaStream_t st, const DecTablesTcArgs& p, int num_sms) {
+  const int64_t tiles = (p.rows + 127) / 128;
+  if (tiles <= 0) return;
+  static bool attr = false;
+  if (!attr) {
+    set_smem(dec_tables_tc_kernel, kTabSmem);
+    attr = true;
+  }
+  const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+  dec_tables_tc_kernel<<<grid, kEncThreads, kTabSmem, st>>>(p);
 }
 
 void launch_enc_edge_tc(cudaStream_t st, const EncEdgeTcArgs& p, int num_sms) {

@@ -815,24 +815,28 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const EncoderOu
   auto& ws = e->ws;
   cudaStream_t st = e->stream;
   const int64_t R = hb.R, SL = R * kK;
+  DecTablesTcArgs ta;
+  ta.h_e = eo.h_e16;
+  ta.rows = SL;
+  ta.err = e->d_err;
   for (int l = 0; l < 3; ++l) {
     uint16_t* pe = ws.get_as<uint16_t>("b.PE" + std::to_string(l), SL * kH);
     uint16_t* pv = ws.get_as<uint16_t>("b.PVenc" + std::to_string(l), R * kH);
     if (!pe || !pv) return {HKB_UNAVAILABLE, "device allocation failed"};
     const std::string q = "dec" + std::to_string(l) + ".";
+    ta.W[l] = e->gemm_img.at(q + "W1b");
+    ta.out[l] = pe;
     LinearTcArgs p;
     p.N = kH;
     p.K = kH;
     p.err = e->d_err;
     p.out_f16 = true;
-    p.M = SL; p.A = eo.h_e16; p.a_f16 = true; p.lda = kH; p.W = e->gemm_img.at(q + "W1b");
-    p.C = pe; p.ldc = kH;
-    launch_linear_tc(st, p, e->num_sms);
-    p.M = R; p.A = eo.h_v; p.a_f16 = false; p.W = e->gemm_img.at(q + "W1d"); p.C = pv;
+    p.M = R; p.A = eo.h_v; p.lda = kH; p.W = e->gemm_img.at(q + "W1d"); p.C = pv; p.ldc = kH;
     launch_linear_tc(st, p, e->num_sms);
     tb->PE[l] = pe;
     tb->PVenc[l] = pv;
   }
+  launch_dec_tables_tc(st, ta, e->num_sms);
   float* a0 = ws.get_as<float>("d.Aenc0", R * kH);
   if (!a0) return {HKB_UNAVAILABLE, "device allocation failed"};
   LinearTcArgs p;
@@ -841,7 +845,7 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const EncoderOu
   launch_linear_tc(st, p, e->num_sms);
   tb->Aenc0 = a0;
   tb->h_enc = eo.h_v;
-  e->launches += 7;
+  e->launches += 5;
   HKB_CUDA(cudaGetLastError());
   return kOk;
 }

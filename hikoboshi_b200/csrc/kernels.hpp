@@ -278,6 +278,16 @@ struct EncFeatTcArgs {
 };
 void launch_enc_featurize_tc(cudaStream_t st, const EncFeatTcArgs& p, int num_sms);
 
+// out[l] = h_E W[l]^T (fp16 [rows,128]) for three 128x128 images in one pass.
+struct DecTablesTcArgs {
+  const uint16_t* h_e = nullptr;
+  int64_t rows = 0;
+  const unsigned char* W[3] = {nullptr, nullptr, nullptr};
+  uint16_t* out[3] = {nullptr, nullptr, nullptr};
+  unsigned int* err = nullptr;
+};
+void launch_dec_tables_tc(cudaStream_t st, const DecTablesTcArgs& p, int num_sms);
+
 int ar_tc_group_size();
 // f32 -> fp16 (f16 = true) or bf16, round to nearest even.
 void convert_f32_to_16(cudaStream_t st, const float* src, uint16_t* dst, int64_t n, bool f16);
