@@ -53,8 +53,22 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
+// GELU in its exact erf form with CUDA's erff.  The tensor-core path rounds
+// every result to fp16, so the reference's own erf approximation (A&S 7.1.26
+// with a table-driven exp, kept by the fp32 parity path) buys nothing here
+// and costs a division and per-lane constant-table lookups.
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+// RBF value f of 16 for the fp16 feature operand: exp(-((d - c_f) / 1.25)^2)
+// with c_f = 2 + f * 20/15 and 2 sigma^2 = 1.5625 (the reference's centres and
+// width, rbf_scalar.cpp:10-35), by the hardware exponential; the relative
+// error (~1e-6) is far below the fp16 rounding of the operand.
+__device__ __forceinline__ float rbf_fast(float dist, int f) {
+  const float c = 2.0f + (float)f * (20.0f / 15.0f);
+  const float dl = dist - c;
+  return __expf(-(dl * dl) * (1.0f / 1.5625f));
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
@@ -200,7 +214,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         const int c = rho * kK + k0 + k;
         const int rj = SJ[c];
         const float nc = rj >= 0 ? p.NAC[(int64_t)rj * 256 + 128 + f] : 0.0f;
-        const float y = rj >= 0 ? gelu_as(v[k] + na + nc) : 0.0f;
+        const float y = rj >= 0 ? gelu_erf(v[k] + na + nc) : 0.0f;
         *reinterpret_cast<__half*>(G + sw128_offset(c, f, kNodeSlots)) = __float2half_rn(y);
       }
     }
@@ -340,10 +354,10 @@ __global__ void __launch_bounds__(kEncThreads, 1)
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const float4 a = na[q], c = nc[q];
-          const float y0 = gelu_as(v[4 * q + 0] + a.x + c.x);
-          const float y1 = gelu_as(v[4 * q + 1] + a.y + c.y);
-          const float y2 = gelu_as(v[4 * q + 2] + a.z + c.z);
-          const float y3 = gelu_as(v[4 * q + 3] + a.w + c.w);
+          const float y0 = gelu_erf(v[4 * q + 0] + a.x + c.x);
+          const float y1 = gelu_erf(v[4 * q + 1] + a.y + c.y);
+          const float y2 = gelu_erf(v[4 * q + 2] + a.z + c.z);
+          const float y3 = gelu_erf(v[4 * q + 3] + a.w + c.w);
           pk[2 * q] = pack_h2(y0, y1);
           pk[2 * q + 1] = pack_h2(y2, y3);
         }
@@ -480,7 +494,7 @@ __device__ __forceinline__ void feat_pair_item(unsigned char* A, int row, int p,
       const float dist =
           pair_distance(a.coords + ((int64_t)r * 5 + ai) * 3, a.coords + ((int64_t)rj * 5 + aj) * 3);
 #pragma unroll
-      for (int f = 0; f < 8; ++f) pk[f] = pack_h2(rbf_value(dist, 2 * f), rbf_value(dist, 2 * f + 1));
+      for (int f = 0; f < 8; ++f) pk[f] = pack_h2(rbf_fast(dist, 2 * f), rbf_fast(dist, 2 * f + 1));
     }
   }
   *reinterpret_cast<uint4*>(A + sw128_offset(row, col, 128)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
