@@ -24,7 +24,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 CU_SOURCES = ["kernels_f32.cu", "kernels_tc.cu", "gemm_tc.cu", "enc_tc.cu", "engine.cu",
               "noalloc.cu"]
-CPP_SOURCES = ["host_order.cpp", "host_synth.cpp", "safetensors.cpp"]
+CPP_SOURCES = ["host_order.cpp", "host_synth.cpp", "safetensors.cpp", "structure_io.cpp",
+               "host_io.cpp"]
 
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
                      "-Xcompiler", "-ffp-contract=off", "--expt-relaxed-constexpr",

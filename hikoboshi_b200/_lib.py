@@ -33,7 +33,15 @@ EXPORTED = ["hkb_mpnn_create", "hkb_mpnn_destroy", "hkb_mpnn_design",
             "hkb_mpnn_design_device", "hkb_mpnn_design_noalloc", "hkb_mpnn_score", "hkb_mpnn_encode",
             "hkb_mpnn_knn", "hkb_mpnn_decode_order", "hkb_synthetic_backbone",
             "hkb_mpnn_last_launch_count", "hkb_mpnn_last_timings",
-            "hkb_mpnn_abi_version"]
+            "hkb_mpnn_abi_version",
+            "hkb_structure_load_file", "hkb_structure_load_text", "hkb_structure_residue_count",
+            "hkb_structure_copy", "hkb_structure_destroy", "hkb_backbone_noise",
+            "hkb_write_design_fasta", "hkb_write_logprobs_npz"]
+
+
+class StructureOptions(ctypes.Structure):
+    _fields_ = [("model_index", c_int32), ("chain_id", c_char_p),
+                ("infer_missing_atoms", c_int32), ("include_modified_residues", c_int32)]
 
 
 class Status(ctypes.Structure):
@@ -113,6 +121,24 @@ def load() -> ctypes.CDLL:
     lib.hkb_mpnn_last_timings.argtypes = [c_void_p, POINTER(c_float)]
     lib.hkb_mpnn_abi_version.restype = c_int32
     lib.hkb_mpnn_abi_version.argtypes = []
+    lib.hkb_structure_load_file.restype = Status
+    lib.hkb_structure_load_file.argtypes = [c_char_p, POINTER(StructureOptions), POINTER(c_void_p)]
+    lib.hkb_structure_load_text.restype = Status
+    lib.hkb_structure_load_text.argtypes = [c_char_p, c_size_t, c_int32, c_char_p,
+                                            POINTER(StructureOptions), POINTER(c_void_p)]
+    lib.hkb_structure_residue_count.restype = c_int32
+    lib.hkb_structure_residue_count.argtypes = [c_void_p]
+    lib.hkb_structure_copy.restype = Status
+    lib.hkb_structure_copy.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p]
+    lib.hkb_structure_destroy.restype = None
+    lib.hkb_structure_destroy.argtypes = [c_void_p]
+    lib.hkb_backbone_noise.restype = Status
+    lib.hkb_backbone_noise.argtypes = [c_int32, c_void_p, c_void_p, c_float, c_uint64, c_void_p]
+    lib.hkb_write_design_fasta.restype = Status
+    lib.hkb_write_design_fasta.argtypes = [c_char_p, c_int32, c_int32, c_void_p, c_void_p,
+                                           c_void_p, c_float, c_int32]
+    lib.hkb_write_logprobs_npz.restype = Status
+    lib.hkb_write_logprobs_npz.argtypes = [c_char_p, c_int32, c_int32, c_void_p]
     _lib = lib
     return lib
 
@@ -123,4 +149,4 @@ def check(st: Status) -> None:
 
 
 __all__ = ["load", "check", "Status", "DesignBatch", "DesignOut", "ScoreBatch", "ScoreOut",
-           "HkbError", "EXPORTED", "c_uint8"]
+           "StructureOptions", "HkbError", "EXPORTED", "c_uint8"]

@@ -206,6 +206,60 @@ hkb_status hkb_mpnn_last_timings(const hkb_engine* engine, float* ms4);
 
 int32_t hkb_mpnn_abi_version(void);
 
+/* ---- host-side input / output of the design command (no device work) ---- */
+
+/* A structure loaded from PDB or mmCIF: one chain of one model, normalised to
+ * the canonical [L,5,3] N/CA/C/O/CB layout with per-atom sources
+ * (0 missing, 1 observed, 2 inferred, 3 virtual).
+ * Replaces io::LoadedStructure / io::load_structure_from_file
+ * (cpp/include/hikoboshi/io/structure_loader.hpp; io/structure_loader.cpp:174-284). */
+typedef struct hkb_structure hkb_structure;
+
+/* io::StructureLoadOptions (structure_loader.hpp:30-38); NULL = defaults. */
+typedef struct {
+  int32_t model_index;               /* 0: model 1 */
+  const char* chain_id;              /* NULL or "": chain A if present, else the first */
+  int32_t infer_missing_atoms;       /* default 1 */
+  int32_t include_modified_residues; /* default 1 (MSE, SEC, PYL, SEP, TPO, PTR, HYP) */
+} hkb_structure_options;
+
+/* Reads a .pdb/.ent/.cif/.mmcif file (format by extension, then content).
+ * Errors carry the reference's codes and detail strings. */
+hkb_status hkb_structure_load_file(const char* path, const hkb_structure_options* options,
+                                   hkb_structure** out);
+/* Same from text; format 0 = detect from content, 1 = PDB, 2 = mmCIF
+ * (io::load_pdb_from_string / load_mmcif_from_string, structure_loader.cpp:202-284). */
+hkb_status hkb_structure_load_text(const char* text, size_t length, int32_t format,
+                                   const char* origin, const hkb_structure_options* options,
+                                   hkb_structure** out);
+int32_t hkb_structure_residue_count(const hkb_structure* structure);
+/* coords f32 [L,5,3], atom_sources u8 [L,5], residue_codes char [L] (any may be NULL). */
+hkb_status hkb_structure_copy(const hkb_structure* structure, float* coords,
+                              uint8_t* atom_sources, char* residue_codes);
+void hkb_structure_destroy(hkb_structure* structure);
+
+/* Backbone noise of one sequence (algorithms/inverse_fold.cpp:191-207): out =
+ * coords + N(0, sigma) on every non-missing atom, drawn x, y, z per atom from
+ * std::mt19937_64(seed ^ 0x4D504E4E76343875) through
+ * std::normal_distribution<float> -- the host's libstdc++, as the reference.
+ * seed is the sequence's seed (base + index); sigma must be finite and >= 0. */
+hkb_status hkb_backbone_noise(int32_t residue_count, const float* coords,
+                              const uint8_t* atom_sources, float sigma, uint64_t seed,
+                              float* out);
+
+/* Design FASTA (io::write_design_fasta, io/design_fasta_writer.cpp:171-199):
+ * ">design_<i> score=<score> seed=<seed> T=<T> decode_order=<random|n_to_c>",
+ * sequences wrapped at 80 columns.  tokens i32 [num_seqs, L]. */
+hkb_status hkb_write_design_fasta(const char* path, int32_t num_seqs, int32_t residue_count,
+                                  const int32_t* tokens, const double* scores,
+                                  const uint64_t* seeds, float sampling_temp,
+                                  int32_t decode_order);
+
+/* Log-prob NPZ (io::write_inverse_fold_logprobs_npz, :201-217): one stored
+ * (uncompressed) ZIP32 member log_probs.npy, float32 [num_seqs, L, 21]. */
+hkb_status hkb_write_logprobs_npz(const char* path, int32_t num_seqs, int32_t residue_count,
+                                  const float* log_probs);
+
 #ifdef __cplusplus
 }
 #endif

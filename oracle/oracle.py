@@ -285,3 +285,54 @@ class RefLib:
         if st != 0:
             raise ValueError(f"reference design failed ({st})")
         return tok, lp, sc
+
+    def design_noisy(self, coords, sources, num_seqs, seed, temperature, backbone_noise,
+                     decode_order=0):
+        """design() with the algorithm layer's backbone_noise (each sequence
+        gets its own noisy copy, algorithms/inverse_fold.cpp:296-302)."""
+        coords, sources = _f32(coords), _u8(sources)
+        L = coords.shape[0]
+        tok = np.zeros((num_seqs, L), np.int32)
+        lp = np.zeros((num_seqs, L, V), np.float32)
+        sc = np.zeros(num_seqs, np.float32)
+        fn = self.lib.ref_design_noisy
+        fn.restype = ctypes.c_int
+        st = fn(_p(coords), _p(sources), ctypes.c_size_t(L), ctypes.c_size_t(num_seqs),
+                ctypes.c_uint64(seed), ctypes.c_float(temperature), ctypes.c_int(decode_order),
+                ctypes.c_float(backbone_noise), _p(tok), _p(lp), _p(sc))
+        if st != 0:
+            raise ValueError(f"reference design failed ({st})")
+        return tok, lp, sc
+
+    def load_structure(self, path, cap=4096):
+        """io::load_structure_from_file -> (code, detail, coords, sources, codes)."""
+        fn = self.lib.ref_load_structure
+        fn.restype = ctypes.c_int
+        self.lib.ref_io_last_detail.restype = ctypes.c_char_p
+        L = ctypes.c_int32(0)
+        c = np.zeros((cap, 5, 3), np.float32)
+        s = np.zeros((cap, 5), np.uint8)
+        codes = ctypes.create_string_buffer(cap)
+        st = fn(str(path).encode(), ctypes.byref(L), _p(c), _p(s), codes, ctypes.c_int32(cap))
+        detail = self.lib.ref_io_last_detail().decode()
+        n = L.value
+        if st != 0:
+            return st, detail, None, None, None
+        return 0, detail, c[:n].copy(), s[:n].copy(), codes.raw[:n].decode()
+
+    def write_fasta(self, path, seqs, scores, seeds, temperature, n_to_c=False):
+        n, L = len(seqs), len(seqs[0]) if seqs else 0
+        buf = "".join(seqs).encode()
+        sc = np.ascontiguousarray(scores, np.float64)
+        sd = np.ascontiguousarray(seeds, np.uint64)
+        fn = self.lib.ref_write_fasta
+        fn.restype = ctypes.c_int
+        return fn(str(path).encode(), ctypes.c_int32(n), ctypes.c_int32(L), buf, _p(sc), _p(sd),
+                  ctypes.c_float(temperature), ctypes.c_int32(int(n_to_c)))
+
+    def write_npz(self, path, log_probs):
+        lp = _f32(log_probs)
+        fn = self.lib.ref_write_npz
+        fn.restype = ctypes.c_int
+        return fn(str(path).encode(), ctypes.c_int32(lp.shape[0]), ctypes.c_int32(lp.shape[1]),
+                  _p(lp))

@@ -20,6 +20,7 @@
 //                           (algorithms/inverse_fold.cpp:221-356): the repo's
 //                           `design` path minus file IO
 //   ref_decode_order        modules::mpnn::proteinmpnn_decode_order_scalar
+//   ref_design_noisy        ref_design with backbone_noise > 0
 //
 // The workspace holders below only size plain std::vectors with the
 // reference's own plan-count helpers; all arithmetic is the reference's.
@@ -363,10 +364,25 @@ int ref_inverse_fold(const float* coords, const std::uint8_t* sources,
 // The algorithms-layer design call: num_seqs sequences with seed+index,
 // decode_order 0 = random, 1 = n_to_c.  Outputs are [num_seqs, L] tokens
 // (as alphabet indices), [num_seqs, L, 21] log-probs, [num_seqs] scores.
+int ref_design_noisy(const float* coords, const std::uint8_t* sources,
+                     std::size_t L, std::size_t num_seqs, std::uint64_t seed,
+                     float temperature, int decode_order, float backbone_noise,
+                     std::int32_t* tokens, float* log_probs, float* scores);
+
 int ref_design(const float* coords, const std::uint8_t* sources,
                std::size_t L, std::size_t num_seqs, std::uint64_t seed,
                float temperature, int decode_order, std::int32_t* tokens,
                float* log_probs, float* scores) {
+  return ref_design_noisy(coords, sources, L, num_seqs, seed, temperature, decode_order, 0.0f,
+                          tokens, log_probs, scores);
+}
+
+// ref_design with the algorithm layer's backbone_noise option
+// (algorithms/inverse_fold.cpp:191-207, 296-302).
+int ref_design_noisy(const float* coords, const std::uint8_t* sources,
+                     std::size_t L, std::size_t num_seqs, std::uint64_t seed,
+                     float temperature, int decode_order, float backbone_noise,
+                     std::int32_t* tokens, float* log_probs, float* scores) {
   if (!g_loaded) return 100;
   hikoboshi::algorithms::InverseFoldRequest req{};
   req.structure.residue_count = L;
@@ -383,6 +399,7 @@ int ref_design(const float* coords, const std::uint8_t* sources,
       decode_order == 1 ? hikoboshi::algorithms::InverseFoldDecodeOrder::NToC
                         : hikoboshi::algorithms::InverseFoldDecodeOrder::Random;
   req.options.keep_log_probs = log_probs != nullptr;
+  req.options.backbone_noise = backbone_noise;
   auto res = hikoboshi::algorithms::inverse_fold_proteinmpnn_v48_020(req);
   if (!res.status.ok()) return static_cast<int>(res.status.code);
   static const char kAlpha[] = "ACDEFGHIKLMNPQRSTVWYX";
