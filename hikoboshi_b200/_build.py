@@ -65,7 +65,27 @@ def build_library(verbose: bool = False) -> Path:
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
+    build_cli(verbose)
     return LIB
+
+
+CLI = PKG / "bin" / "hikoboshi"
+
+
+def build_cli(verbose: bool = False) -> Path:
+    """`hikoboshi design` (csrc/cli_design.cpp over include/hkb_design_api.hpp),
+    linked to the in-tree library through an $ORIGIN-relative rpath."""
+    src = CSRC / "cli_design.cpp"
+    deps = [src, LIB, ROOT / "include" / "hkb_design_api.hpp", ROOT / "include" / "hkb_mpnn.h"]
+    if CLI.exists() and CLI.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
+        return CLI
+    CLI.parent.mkdir(exist_ok=True)
+    cmd = [shutil.which("g++") or "g++", "-std=c++17", "-O2", "-Wall", f"-I{ROOT / 'include'}",
+           str(src), "-o", str(CLI), f"-L{PKG}", "-lhkb_mpnn", "-Wl,-rpath,$ORIGIN/.."]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return CLI
 
 
 WEIGHTS_NAME = "Hikoboshi-ProteinMPNN-v48-020.safetensors"
