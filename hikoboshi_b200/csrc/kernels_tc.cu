@@ -399,9 +399,11 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           const float4 a0 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2];
           const float4 a1 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2 + 1];
           const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+          // the operand holds 2 GELU(x): the epilogue halves D2 when it adds
+          // b2 (W2 is linear and a power-of-two scale is exact)
           float y[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) y[q] = gelu_tc(av[q] + tsum[q]);
+          for (int q = 0; q < 8; ++q) y[q] = gelu2_tc(av[q] + tsum[q]);
           outv = make_uint4(pack16<F16>(y[0], y[1]), pack16<F16>(y[2], y[3]),
                             pack16<F16>(y[4], y[5]), pack16<F16>(y[6], y[7]));
         }
@@ -498,14 +500,14 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
             tmem_ld32(tm + lane_base + kColD2 + bf * kChunkN + sub * kK, v);
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (i < K) acc[i & 3] += gelu2_tc(v[i] + b2);
+              if (i < K) acc[i & 3] += gelu2_tc(fmaf(v[i], 0.5f, b2));
           }
           {
             float v[16];
             tmem_ld16(tm + lane_base + kColD2 + bf * kChunkN + sub * kK + 32, v);
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-              if (i + 32 < K) acc[i & 3] += gelu2_tc(v[i] + b2);
+              if (i + 32 < K) acc[i & 3] += gelu2_tc(fmaf(v[i], 0.5f, b2));
           }
           const float total = 0.5f * ((acc[0] + acc[1]) + (acc[2] + acc[3]));
           if (s < n)
