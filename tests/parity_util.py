@@ -23,10 +23,19 @@ def check_design(oracle, coords, sources, tokens, log_probs, order, seed, temper
     """cdf_tol=None bounds the CDF shift by the observed log-prob error: with
     |d log p_v| <= e for every v, each CDF boundary moves by at most
     sum_v p_v |exp(d log p_v) - 1| <= exp(e) - 1."""
-    L = coords.shape[0]
     mask = (sources[:, :4].min(axis=1) > 0)
-    assert sorted(order.tolist()) == list(range(L))
     ref = oracle.teacher_forced_scaled(coords, sources, tokens, order, temperature)
+    return check_against(oracle.uniform, ref, mask, tokens, log_probs, order, seed, temperature,
+                         lp_tol, cdf_tol)
+
+
+def check_against(uniform, ref, mask, tokens, log_probs, order, seed, temperature, lp_tol,
+                  cdf_tol=None):
+    """check_design with the reference's scaled log-probs `ref` [L,21] given
+    (e.g. from a teacher-forced pass of the fp32 engine) and `uniform(seed, i)`
+    the sampler's draw stream."""
+    L = ref.shape[0]
+    assert sorted(order.tolist()) == list(range(L))
     act = mask
     err = 0.0
     if act.any():
@@ -51,7 +60,7 @@ def check_design(oracle, coords, sources, tokens, log_probs, order, seed, temper
                 assert top[1] - top[0] <= cdf_tol, (p, t, tokens[t], best)
                 boundary_hits += 1
             continue
-        u = oracle.uniform(seed, draw)
+        u = uniform(seed, draw)
         draw += 1
         probs = np.exp(lp.astype(np.float64))
         probs = probs / probs.sum()
