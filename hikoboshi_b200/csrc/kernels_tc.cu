@@ -71,7 +71,8 @@ constexpr uint32_t kOffNb = kOffXs + kGB * kH * 4;              // int [16,48]
 constexpr uint32_t kOffLogit = kOffNb + kGB * kK * 4;           // float [16,32]
 constexpr uint32_t kOffStab = kOffLogit + kGB * 32 * 4;         // 16-bit [3,21,128]
 constexpr uint32_t kOffHead = kOffStab + 16384;                 // fp32 [128,21]
-constexpr uint32_t kOffMisc = kOffHead + kH * kV * 4;
+constexpr uint32_t kOffNbNext = kOffHead + kH * kV * 4;        // int [16,48] next position
+constexpr uint32_t kOffMisc = kOffNbNext + kGB * kK * 4;
 constexpr uint32_t kSmemBytes = kOffMisc + 1024 + 1024;         // + misc + alignment slack
 
 struct Misc {
@@ -87,6 +88,9 @@ struct Misc {
   unsigned long long rng[kGB];
   float temp[kGB];
   int off[kGB];   // first residue row of the sequence's protein
+  int t_next[kGB];     // next position's residue and mask (prefetched)
+  float m_next[kGB];
+  int tok_cur[kGB];    // token sampled at the current position
 };
 static_assert(sizeof(Misc) <= 1024, "misc block");
 
@@ -213,6 +217,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   float (*Aa)[kH] = reinterpret_cast<float (*)[kH]>(sm + kOffAa);
   float (*Xs)[kH] = reinterpret_cast<float (*)[kH]>(sm + kOffXs);
   int (*Nb)[kK] = reinterpret_cast<int (*)[kK]>(sm + kOffNb);
+  int (*NbNext)[kK] = reinterpret_cast<int (*)[kK]>(sm + kOffNbNext);
   float (*Lg)[32] = reinterpret_cast<float (*)[32]>(sm + kOffLogit);
   uint16_t* StabS = reinterpret_cast<uint16_t*>(sm + kOffStab);
   float* HeadS = reinterpret_cast<float*>(sm + kOffHead);
@@ -297,39 +302,66 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     // uniform exit: every thread takes the same branch
     if (__syncthreads_or(M.abort_flag)) break;
     // ---- per-position set-up ------------------------------------------------
-    if (tid < kGB) {
-      int t = 0;
-      float m = 0.0f;
-      if (tid < n) {
-        t = a.orders[M.qrow[tid] + p];
-        t = (t < 0 || t >= L) ? 0 : t;
-        m = a.mask[M.off[tid] + t];
+    // Position 0 reads everything here; later positions take the residue, the
+    // mask and the neighbour codes prefetched during the previous position's
+    // last layer (only the token decoded there is filled in now).
+    constexpr int kFresh = 1 << 30;   // neighbour decoded at the previous position
+    if (p == 0) {
+      if (tid < kGB) {
+        int t = 0;
+        float m = 0.0f;
+        if (tid < n) {
+          t = a.orders[M.qrow[tid] + p];
+          t = (t < 0 || t >= L) ? 0 : t;
+          m = a.mask[M.off[tid] + t];
+        }
+        M.t[tid] = t;
+        M.m[tid] = m;
       }
-      M.t[tid] = t;
-      M.m[tid] = m;
+      __syncthreads();
+      for (int e = tid; e < n * kK; e += kThreadsB) {
+        const int s = e / kK, k = e % kK;
+        int code = 0;
+        if (k < K) {
+          const int64_t rt = M.off[s] + M.t[s];
+          int j = a.e_idx[rt * kK + k];
+          if (j < 0 || j >= L) {
+            atomicOr(err, kErrBadIndex);
+            j = M.t[s];
+          }
+          code = j;   // nothing is decoded before position 0
+        }
+        Nb[s][k] = code;
+      }
+    } else {
+      if (tid < kGB) {
+        M.t[tid] = M.t_next[tid];
+        M.m[tid] = M.m_next[tid];
+      }
+      for (int e = tid; e < n * kK; e += kThreadsB) {
+        const int s = e / kK, k = e % kK;
+        int code = NbNext[s][k];
+        if (code & kFresh) code = (code & ~kFresh) | (M.tok_cur[s] << 17);
+        Nb[s][k] = code;
+      }
+      __syncthreads();
     }
-    __syncthreads();
     for (int e = tid; e < kGB * kH; e += kThreadsB) {
       const int s = e >> 7, f = e & 127;
       hS[s][f] = s < n ? tb.h_enc[(int64_t)(M.off[s] + M.t[s]) * kH + f] : 0.0f;
       Aa[s][f] = s < n ? tb.Aenc0[(int64_t)(M.off[s] + M.t[s]) * kH + f] : 0.0f;
     }
-    for (int e = tid; e < n * kK; e += kThreadsB) {
-      const int s = e / kK, k = e % kK;
-      int code = 0;
-      if (k < K) {
-        const int64_t rt = M.off[s] + M.t[s];
-        int j = a.e_idx[rt * kK + k];
-        if (j < 0 || j >= L) {
-          atomicOr(err, kErrBadIndex);
-          j = M.t[s];
-        }
-        const int64_t qj = M.qrow[s] + j;
-        const bool bw = a.pos[qj] < p;
-        const int tok = bw ? a.tokens[qj] : 0;
-        code = j | (bw ? (1 << 16) : 0) | (tok << 17);
+    // the next position's residue and mask, for the prefetch in layer 2
+    if (tid < kGB) {
+      int t = 0;
+      float m = 0.0f;
+      if (tid < n && p + 1 < L) {
+        t = a.orders[M.qrow[tid] + p + 1];
+        t = (t < 0 || t >= L) ? 0 : t;
+        m = a.mask[M.off[tid] + t];
       }
-      Nb[s][k] = code;
+      M.t_next[tid] = t;
+      M.m_next[tid] = m;
     }
     __syncthreads();
 
@@ -563,6 +595,35 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       }
       fence_async_smem();
       __syncthreads();
+      // ---- last layer: the next position's neighbour codes (its residue and
+      // mask were read at this position's set-up) and an L2 prefetch of its
+      // node rows; they are consumed after this position's sampling.
+      if (l == 2 && p + 1 < L) {
+        for (int e = tid; e < n * kK; e += kThreadsB) {
+          const int s = e / kK, k = e % kK;
+          int code = 0;
+          if (k < K) {
+            const int tn = M.t_next[s];
+            int j = a.e_idx[(int64_t)(M.off[s] + tn) * kK + k];
+            if (j < 0 || j >= L) {
+              atomicOr(err, kErrBadIndex);
+              j = tn;
+            }
+            const int64_t qj = M.qrow[s] + j;
+            const int ps = a.pos[qj];
+            if (ps < p) code = j | (1 << 16) | (a.tokens[qj] << 17);
+            else if (ps == p) code = j | (1 << 16) | kFresh;   // decoded at this position
+            else code = j;
+          }
+          NbNext[s][k] = code;
+        }
+        if (tid < n * 8) {
+          const int s = tid >> 3, line = tid & 3;
+          const float* row = ((tid >> 2) & 1 ? tb.Aenc0 : tb.h_enc) +
+                             (int64_t)(M.off[s] + M.t_next[s]) * kH + line * 32;
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(row));
+        }
+      }
       // ---- FFN: DO = sum_i W_out[:, i] GELU(W_in[i] h1 + b_in[i]) ----------
       for (int i = 0; i < 4; ++i) {
         if (tid == 0) {
@@ -713,7 +774,10 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           if (hit) tok = __ffs(hit) - 1;
         }
       }
-      if (lane == 0) a.tokens[q] = tok;
+      if (lane == 0) {
+        a.tokens[q] = tok;
+        M.tok_cur[s] = tok;
+      }
     }
     __syncthreads();
   }
