@@ -115,6 +115,20 @@ __device__ __forceinline__ float gelu2_tc(float x) {
 }
 __device__ __forceinline__ float gelu_tc(float x) { return 0.5f * gelu2_tc(x); }
 
+// gelu2_tc on two values at once through the packed fp32 pipe (mul / fma
+// .f32x2): each lane takes the same roundings in the same order as the scalar
+// form, so the results are identical, at about half the FP32 issue slots.
+__device__ __forceinline__ float2 gelu2_tc_x2(const float2 x) {
+  float2 x2 = __fmul2_rn(x, x);
+  x2.x = fminf(x2.x, 25.0f);
+  x2.y = fminf(x2.y, 25.0f);
+  float2 p = __ffma2_rn(make_float2(-3.51516790e-04f, -3.51516790e-04f), x2,
+                        make_float2(3.70056460e-02f, 3.70056460e-02f));
+  p = __ffma2_rn(p, x2, make_float2(7.97507884e-01f, 7.97507884e-01f));
+  const float2 u = __fmul2_rn(x, p);
+  return __ffma2_rn(x, make_float2(tanh_approx(u.x), tanh_approx(u.y)), x);
+}
+
 template <bool F16>
 __device__ __forceinline__ uint32_t pack16(float a, float b) {
   if constexpr (F16) {
@@ -433,11 +447,13 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
           // the operand holds 2 GELU(x): the epilogue halves D2 when it adds
           // b2 (W2 is linear and a power-of-two scale is exact)
-          float y[8];
+          float2 y[4];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) y[q] = gelu2_tc(av[q] + tsum[q]);
-          outv = make_uint4(pack16<F16>(y[0], y[1]), pack16<F16>(y[2], y[3]),
-                            pack16<F16>(y[4], y[5]), pack16<F16>(y[6], y[7]));
+          for (int q = 0; q < 4; ++q)
+            y[q] = gelu2_tc_x2(__fadd2_rn(make_float2(av[2 * q], av[2 * q + 1]),
+                                          make_float2(tsum[2 * q], tsum[2 * q + 1])));
+          outv = make_uint4(pack16<F16>(y[0].x, y[0].y), pack16<F16>(y[1].x, y[1].y),
+                            pack16<F16>(y[2].x, y[2].y), pack16<F16>(y[3].x, y[3].y));
         }
         *reinterpret_cast<uint4*>(dst + sw128_offset(r, c8 * 8, kChunkN)) = outv;
       }
@@ -525,23 +541,31 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           tc_fence_after();
           const int s = c * kChunkSeqs + sub;
           // four interleaved partial sums (a 48-long dependent add chain
-          // would dominate), combined in a fixed order
-          float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          // would dominate), combined in a fixed order: slot i adds into
+          // partial i mod 4, i.e. lane i mod 2 of pair (i mod 4) / 2.
+          // Slots past K add an exact zero.
+          float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+          const float2 half2c = make_float2(0.5f, 0.5f), b2p = make_float2(b2, b2);
+          auto sum_pairs = [&](const float* v, int n_pairs, int i0) {
+#pragma unroll
+            for (int m = 0; m < n_pairs; ++m) {
+              float2 gv = gelu2_tc_x2(__ffma2_rn(make_float2(v[2 * m], v[2 * m + 1]), half2c, b2p));
+              if (i0 + 2 * m >= K) gv.x = 0.0f;
+              if (i0 + 2 * m + 1 >= K) gv.y = 0.0f;
+              acc[m & 1] = __fadd2_rn(acc[m & 1], gv);
+            }
+          };
           {
             float v[32];
             tmem_ld32(tm + lane_base + kColD2 + bf * kChunkN + sub * kK, v);
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < K) acc[i & 3] += gelu2_tc(fmaf(v[i], 0.5f, b2));
+            sum_pairs(v, 16, 0);
           }
           {
             float v[16];
             tmem_ld16(tm + lane_base + kColD2 + bf * kChunkN + sub * kK + 32, v);
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (i + 32 < K) acc[i & 3] += gelu2_tc(fmaf(v[i], 0.5f, b2));
+            sum_pairs(v, 8, 32);
           }
-          const float total = 0.5f * ((acc[0] + acc[1]) + (acc[2] + acc[3]));
+          const float total = 0.5f * ((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y));
           if (s < n)
             *reinterpret_cast<uint16_t*>(sm + kOffSb + sw128_offset(s, feat, kGB)) =
                 to16<F16>(total);
