@@ -25,7 +25,8 @@ constexpr int kGemmThreads = 256;
 constexpr uint32_t kAChunkBytes = 128 * 128 * 2;   // 32 KiB per K chunk
 
 template <bool AF16>
-__global__ void __launch_bounds__(kGemmThreads, 1) linear_tc_kernel(LinearTcArgs p) {
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    linear_tc_kernel(const __grid_constant__ LinearTcArgs p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int Kp = (p.K + 63) & ~63;                       // padded K (atoms)
@@ -69,10 +70,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) linear_tc_kernel(LinearTcArgs
       bulk_g2s(sW + o, p.W + o, n, &bar_w);
     }
   }
-  uint32_t ph_a[2] = {0, 0};
+  uint32_t ph_a = 0;     // bit b: parity of A buffer b's next barrier phase
   uint32_t ph_d = 0;
   bool w_ready = false;
-  int used[2] = {0, 0};   // MMA groups committed on each A buffer (same on all threads)
+  // bit b: an MMA group committed on A buffer b is still owed its wait (same on
+  // all threads; bit masks rather than arrays indexed by b, which would sit in
+  // local memory)
+  uint32_t owed = 0;
 
   const int64_t tiles = (p.M + 127) / 128;
   for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -81,10 +85,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) linear_tc_kernel(LinearTcArgs
     for (int c = 0; c < nchunks; ++c) {
       const int b = c & 1;
       // the MMAs that last read buffer b must be done before it is refilled
-      if (used[b] > 0) {
-        if (!mbar_wait(&bar_a[b], ph_a[b], p.err)) abort_flag = 1;
-        ph_a[b] ^= 1;
-        --used[b];
+      if ((owed >> b) & 1u) {
+        if (!mbar_wait(&bar_a[b], (ph_a >> b) & 1u, p.err)) abort_flag = 1;
+        ph_a ^= 1u << b;
+        owed &= ~(1u << b);
       }
       unsigned char* dst = sA + b * kAChunkBytes;
       const int k0 = c * kchunk;
@@ -146,7 +150,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) linear_tc_kernel(LinearTcArgs
         mma_commit(&bar_a[b]);
         if (c == nchunks - 1) mma_commit(&bar_d);
       }
-      ++used[b];
+      owed |= 1u << b;
     }
     // epilogue: wait for the accumulator, then rows out
     if (!mbar_wait(&bar_d, ph_d, p.err)) abort_flag = 1;
@@ -192,10 +196,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) linear_tc_kernel(LinearTcArgs
   }
   // drain the A-buffer barriers still owed a wait, then the weight load
   for (int b = 0; b < 2; ++b)
-    while (used[b] > 0) {
-      mbar_wait(&bar_a[b], ph_a[b], p.err);
-      ph_a[b] ^= 1;
-      --used[b];
+    if ((owed >> b) & 1u) {
+      mbar_wait(&bar_a[b], (ph_a >> b) & 1u, p.err);
+      ph_a ^= 1u << b;
     }
   if (tid == 0 && !w_ready) mbar_wait(&bar_w, 0, p.err);
   tc_fence_before();

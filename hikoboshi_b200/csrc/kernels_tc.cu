@@ -223,7 +223,9 @@ __device__ __forceinline__ uint32_t stream_wait(long long j, unsigned char* sm, 
 
 template <bool F16>
 __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
-    BatchView bv, Bf16DecodeWeights w, Bf16DecodeTables tb, ArBf16Args a, unsigned int* err) {
+    const __grid_constant__ BatchView bv, const __grid_constant__ Bf16DecodeWeights w,
+    const __grid_constant__ Bf16DecodeTables tb, const __grid_constant__ ArBf16Args a,
+    unsigned int* err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Misc& M = *reinterpret_cast<Misc*>(sm + kOffMisc);
@@ -308,7 +310,9 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   const bool producer = warp < kProducerWarps;
   volatile int* abort_p = &M.abort_flag;
   uint4 raw_pe[kRowsPerThread], raw_v[kRowsPerThread];   // in-flight slot rows (producers)
-  uint32_t buf_use[2] = {0, 0};   // chunks issued on each D2 / operand buffer so far
+  // chunks issued on D2 / operand buffer 0 and 1 so far (two scalars: an
+  // array indexed by the buffer would live in local memory)
+  uint32_t use0 = 0, use1 = 0;
   uint32_t ph_all = 0;
   long long tile = 0;   // next tile to consume (same on all threads)
 
@@ -507,17 +511,18 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         uint32_t wa = 0;
         for (int c = 0; c < nch; ++c) {
           const int bf = c & 1;
+          const uint32_t used = bf ? use1 : use0;
           // operand buffer bf is free once the MMA that last read it completed
-          if (buf_use[bf] > 0 && !*abort_p &&
-              !mbar_wait_abortable(&M.bar_d2[bf], (buf_use[bf] - 1) & 1, err, abort_p))
+          if (used > 0 && !*abort_p &&
+              !mbar_wait_abortable(&M.bar_d2[bf], (used - 1) & 1, err, abort_p))
             *abort_p = 1;
           build_operand(c, StabL, raw_pe, raw_v);
           fence_async_smem();
           named_bar_sync(1, kProducerThreads);
           if (tid == 0) {
             if (c == 0) wa = stream_wait(tile, sm, M, err);
-            if (buf_use[bf] > 0 && !*abort_p &&
-                !mbar_wait_abortable(&M.bar_free[bf], (buf_use[bf] - 1) & 1, err, abort_p))
+            if (used > 0 && !*abort_p &&
+                !mbar_wait_abortable(&M.bar_free[bf], (used - 1) & 1, err, abort_p))
               *abort_p = 1;
             tc_fence_after();
             if (!*abort_p)
@@ -526,18 +531,30 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
                        idesc16<F16>(128, kChunkN), false);
             mma_commit(&M.bar_d2[bf]);
           }
-          ++buf_use[bf];
+          if (bf) ++use1; else ++use0;
           if (c + 1 < nch) load_rows(c + 1, l, raw_pe, raw_v);
           else if (l < 2) load_rows(0, l + 1, raw_pe, raw_v);
         }
       } else {
+        // The PE rows (W1b h_E: K contiguous rows per sequence) of the next
+        // message phase -- layer l+1 here, or layer 0 at the next position --
+        // are prefetched into L2 a whole layer ahead: the table is far larger
+        // than L2 and each row is read once per sequence, so these gathers
+        // would otherwise wait on DRAM.
+        if (tid - kProducerThreads < n && (l < 2 || p + 1 < L)) {
+          const int s = tid - kProducerThreads;
+          const int t = l < 2 ? M.t[s] : M.t_next[s];
+          bulk_prefetch_l2(tb.PE[l < 2 ? l + 1 : 0] + (int64_t)(M.off[s] + t) * kK * kH,
+                           (uint32_t)(K * kH * 2));
+        }
         const int sub = (warp - kProducerWarps) >> 2;   // sequence of the chunk
         const float b2 = w.b2[l][feat];
         for (int c = 0; c < nch; ++c) {
           const int bf = c & 1;
-          if (!*abort_p && !mbar_wait_abortable(&M.bar_d2[bf], buf_use[bf] & 1, err, abort_p))
+          if (!*abort_p &&
+              !mbar_wait_abortable(&M.bar_d2[bf], (bf ? use1 : use0) & 1, err, abort_p))
             *abort_p = 1;
-          ++buf_use[bf];
+          if (bf) ++use1; else ++use0;
           tc_fence_after();
           const int s = c * kChunkSeqs + sub;
           // four interleaved partial sums (a 48-long dependent add chain

@@ -124,6 +124,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// L2 prefetch of a contiguous global range (both the address and the size a
+// multiple of 16 bytes); nothing waits on it.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Generic-proxy shared-memory writes become visible to the async proxy
 // (tensor cores, bulk copies).
 __device__ __forceinline__ void fence_async_smem() {
