@@ -18,13 +18,13 @@
 //
 // Weight tiles stream through a 3-slot shared-memory ring by 1-D bulk copies
 // (no tensor map) issued by thread 0 in consumption order.  The CTA has 16
-// warps.  In the message (slot) phase they split into 8 producer warps, which
-// gather neighbour rows (one chunk ahead, in registers), build the GELU
-// operand and issue the MMA, and 8 epilogue warps, which sum GELU(D2 + b2)
-// over the slots; the roles hand buffers to each other through mbarriers, so
-// the two GELU passes of consecutive chunks overlap.  All 16 warps share the
-// node, LayerNorm, FFN and sampling phases.  Every wait is bounded; a timeout
-// sets the error word and the CTA stops.
+// warps.  In the message (slot) phase they form two ping-pong groups of 8
+// warps; each group gathers the neighbour rows of its next chunk (in
+// registers, one chunk ahead), builds the GELU operand, issues the MMA and
+// sums GELU(D2 + b2) over the slots of its own chunks, so that one group's
+// MMA wait and slot sum overlap the other group's gather and build.  All 16
+// warps share the node, LayerNorm, FFN and sampling phases.  Every wait is
+// bounded; a timeout sets the error word and the CTA stops.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -43,9 +43,7 @@ constexpr int kChunkN = kChunkSeqs * kK;  // 96 neighbour slots
 constexpr int kSlots = 3;         // weight ring depth
 constexpr int kThreadsB = 512;
 constexpr int kWarpsB = kThreadsB / 32;
-constexpr int kProducerWarps = 8;  // warps 0-7: slot gather, operand build, MMA issue
-constexpr int kProducerThreads = kProducerWarps * 32;
-// warps 8-15: slot-sum epilogue (two warps per TMEM lane quadrant)
+constexpr int kGroupThreads = 256;  // message-phase ping-pong group: warps 0-7 / 8-15
 
 // TMEM columns (fp32 accumulators, lanes = output features)
 constexpr uint32_t kColD2 = 0;    // 2 x 96
@@ -77,8 +75,7 @@ constexpr uint32_t kSmemBytes = kOffMisc + 1024 + 1024;         // + misc + alig
 
 struct Misc {
   uint64_t full[kSlots];
-  uint64_t bar_d2[2];     // message MMA of a chunk complete (D2 buffer full)
-  uint64_t bar_free[2];   // epilogue warps done reading a D2 buffer
+  uint64_t bar_d2[2];     // message MMA of group g's chunk complete (D2 buffer g full)
   uint64_t bar_all;
   uint32_t tbase;
   int abort_flag;
@@ -259,8 +256,6 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     for (int i = 0; i < kSlots; ++i) mbar_init(&M.full[i], 1);
     mbar_init(&M.bar_d2[0], 1);
     mbar_init(&M.bar_d2[1], 1);
-    mbar_init(&M.bar_free[0], kWarpsB - kProducerWarps);
-    mbar_init(&M.bar_free[1], kWarpsB - kProducerWarps);
     mbar_init(&M.bar_all, 1);
     M.abort_flag = 0;
     fence_barrier_init();
@@ -306,13 +301,14 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     }
   __syncthreads();
 
-  constexpr int kRowsPerThread = kChunkN / 16;
-  const bool producer = warp < kProducerWarps;
+  // a group thread owns one 8-feature column chunk of this many slot rows
+  constexpr int kRowsPerThread = kChunkN * 16 / kGroupThreads;
+  const int grp = tid / kGroupThreads;       // ping-pong group of the message phase
+  const int gtid = tid % kGroupThreads;
+  const int sub = (warp >> 2) & 1;           // sequence of a chunk this warp sums
   volatile int* abort_p = &M.abort_flag;
-  uint4 raw_pe[kRowsPerThread], raw_v[kRowsPerThread];   // in-flight slot rows (producers)
-  // chunks issued on D2 / operand buffer 0 and 1 so far (two scalars: an
-  // array indexed by the buffer would live in local memory)
-  uint32_t use0 = 0, use1 = 0;
+  uint4 raw_pe[kRowsPerThread], raw_v[kRowsPerThread];   // in-flight slot rows
+  uint32_t d2_count = 0;   // this group's message MMAs waited for so far
   uint32_t ph_all = 0;
   long long tile = 0;   // next tile to consume (same on all threads)
 
@@ -383,13 +379,13 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     }
     __syncthreads();
 
-    // Row loads of one neighbour-slot chunk (producer threads): a thread owns
+    // Row loads of one neighbour-slot chunk (a ping-pong group): a thread owns
     // one 8-feature column chunk (tid % 16) of six slot rows (W1b h_E row and
     // the neighbour's W1d h row, 16-bit).
     auto load_rows = [&](int c, int layer, uint4 (&pe_raw)[kRowsPerThread],
                          uint4 (&v_raw)[kRowsPerThread]) {
       const int c8 = tid & 15;
-      const int r0 = tid >> 4;
+      const int r0 = gtid >> 4;
       const uint16_t* PE = tb.PE[layer];
       const uint16_t* PVenc = tb.PVenc[layer];
       const uint16_t* PVl =
@@ -420,7 +416,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
                              const uint4 (&v_raw)[kRowsPerThread]) {
       unsigned char* dst = sm + kOffG1 + (c & 1) * kG1Bytes;
       const int c8 = tid & 15;
-      const int r0 = tid >> 4;
+      const int r0 = gtid >> 4;
 #pragma unroll
       for (int i = 0; i < kRowsPerThread; ++i) {
         const int r = r0 + 16 * i;
@@ -462,7 +458,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         *reinterpret_cast<uint4*>(dst + sw128_offset(r, c8 * 8, kChunkN)) = outv;
       }
     };
-    if (producer) load_rows(0, 0, raw_pe, raw_v);      // chunk 0 of layer 0
+    load_rows(grp, 0, raw_pe, raw_v);          // this group's first chunk of layer 0
 
     for (int l = 0; l < 3; ++l) {
       if (__syncthreads_or(M.abort_flag)) break;
@@ -499,70 +495,59 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         __syncthreads();
       }
       // ---- messages: gather + GELU -> W2 MMA -> GELU + slot sum ------------
-      // Producer warps build chunk c's operand (rows prefetched into registers
-      // one chunk ahead; chunk 0 of the next layer is fetched during this
-      // layer's W3 / FFN phases) and issue its MMA; epilogue warps sum
-      // GELU(D2 + b2) over the slots of chunk c-1 meanwhile.  Two D2 / operand
-      // buffers; bar_d2 hands a full D2 to the epilogue (and frees the operand
-      // buffer), bar_free hands the D2 buffer back.
+      // Two ping-pong groups of 8 warps; group g takes chunks g, g+2, ... and
+      // owns operand buffer g and D2 buffer g.  Per chunk a group builds the
+      // operand from rows already in registers, one elected thread issues
+      // the MMA, the group issues the row loads of its next chunk (chunk g
+      // of the next layer after its last one; they stay in flight through
+      // the W3 / FFN phases), then waits for D2 and sums GELU(D2 + b2) over
+      // the slots.  While one group waits on its MMA or sums, the other
+      // builds, so the two halves of the work overlap without handing
+      // buffers across groups.
       const int nch = (n + kChunkSeqs - 1) / kChunkSeqs;
-      if (producer) {
-        const uint16_t* StabL = StabS + l * kV * kH;
-        uint32_t wa = 0;
-        for (int c = 0; c < nch; ++c) {
-          const int bf = c & 1;
-          const uint32_t used = bf ? use1 : use0;
-          // operand buffer bf is free once the MMA that last read it completed
-          if (used > 0 && !*abort_p &&
-              !mbar_wait_abortable(&M.bar_d2[bf], (used - 1) & 1, err, abort_p))
-            *abort_p = 1;
-          build_operand(c, StabL, raw_pe, raw_v);
-          fence_async_smem();
-          named_bar_sync(1, kProducerThreads);
-          if (tid == 0) {
-            if (c == 0) wa = stream_wait(tile, sm, M, err);
-            if (used > 0 && !*abort_p &&
-                !mbar_wait_abortable(&M.bar_free[bf], (used - 1) & 1, err, abort_p))
-              *abort_p = 1;
-            tc_fence_after();
-            if (!*abort_p)
-              mma_k128(tm + kColD2 + bf * kChunkN, wa,
-                       smem_u32(sm + kOffG1 + bf * kG1Bytes), kChunkN,
-                       idesc16<F16>(128, kChunkN), false);
-            mma_commit(&M.bar_d2[bf]);
-          }
-          if (bf) ++use1; else ++use0;
-          if (c + 1 < nch) load_rows(c + 1, l, raw_pe, raw_v);
-          else if (l < 2) load_rows(0, l + 1, raw_pe, raw_v);
-        }
-      } else {
+      {
         // The PE rows (W1b h_E: K contiguous rows per sequence) of the next
         // message phase -- layer l+1 here, or layer 0 at the next position --
         // are prefetched into L2 a whole layer ahead: the table is far larger
         // than L2 and each row is read once per sequence, so these gathers
         // would otherwise wait on DRAM.
-        if (tid - kProducerThreads < n && (l < 2 || p + 1 < L)) {
-          const int s = tid - kProducerThreads;
-          const int t = l < 2 ? M.t[s] : M.t_next[s];
-          bulk_prefetch_l2(tb.PE[l < 2 ? l + 1 : 0] + (int64_t)(M.off[s] + t) * kK * kH,
+        if (grp == 1 && gtid < n && (l < 2 || p + 1 < L)) {
+          const int t = l < 2 ? M.t[gtid] : M.t_next[gtid];
+          bulk_prefetch_l2(tb.PE[l < 2 ? l + 1 : 0] + (int64_t)(M.off[gtid] + t) * kK * kH,
                            (uint32_t)(K * kH * 2));
         }
-        const int sub = (warp - kProducerWarps) >> 2;   // sequence of the chunk
+        const uint16_t* StabL = StabS + l * kV * kH;
+        const float2 half2c = make_float2(0.5f, 0.5f);
         const float b2 = w.b2[l][feat];
-        for (int c = 0; c < nch; ++c) {
-          const int bf = c & 1;
-          if (!*abort_p &&
-              !mbar_wait_abortable(&M.bar_d2[bf], (bf ? use1 : use0) & 1, err, abort_p))
+        const float2 b2p = make_float2(b2, b2);
+        const uint32_t d2col = kColD2 + grp * kChunkN + sub * kK;
+        uint32_t wa = 0;
+        for (int c = grp; c < nch; c += 2) {
+          // Operand / D2 buffer grp is free: this group waited for its last
+          // MMA and read its D2 before arriving at the barrier below.
+          build_operand(c, StabL, raw_pe, raw_v);
+          fence_async_smem();
+          named_bar_sync(1 + grp, kGroupThreads);
+          if (gtid == 0) {
+            if (c == grp) wa = stream_wait(tile, sm, M, err);
+            tc_fence_after();
+            if (!*abort_p)
+              mma_k128(tm + kColD2 + grp * kChunkN, wa,
+                       smem_u32(sm + kOffG1 + grp * kG1Bytes), kChunkN,
+                       idesc16<F16>(128, kChunkN), false);
+            mma_commit(&M.bar_d2[grp]);
+          }
+          if (c + 2 < nch) load_rows(c + 2, l, raw_pe, raw_v);
+          else if (l < 2) load_rows(grp, l + 1, raw_pe, raw_v);
+          if (!*abort_p && !mbar_wait_abortable(&M.bar_d2[grp], d2_count & 1, err, abort_p))
             *abort_p = 1;
-          if (bf) ++use1; else ++use0;
+          ++d2_count;
           tc_fence_after();
-          const int s = c * kChunkSeqs + sub;
           // four interleaved partial sums (a 48-long dependent add chain
           // would dominate), combined in a fixed order: slot i adds into
           // partial i mod 4, i.e. lane i mod 2 of pair (i mod 4) / 2.
           // Slots past K add an exact zero.
           float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-          const float2 half2c = make_float2(0.5f, 0.5f), b2p = make_float2(b2, b2);
           auto sum_pairs = [&](const float* v, int n_pairs, int i0) {
 #pragma unroll
             for (int m = 0; m < n_pairs; ++m) {
@@ -574,21 +559,20 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           };
           {
             float v[32];
-            tmem_ld32(tm + lane_base + kColD2 + bf * kChunkN + sub * kK, v);
+            tmem_ld32(tm + lane_base + d2col, v);
             sum_pairs(v, 16, 0);
           }
           {
             float v[16];
-            tmem_ld16(tm + lane_base + kColD2 + bf * kChunkN + sub * kK + 32, v);
+            tmem_ld16(tm + lane_base + d2col + 32, v);
             sum_pairs(v, 8, 32);
           }
           const float total = 0.5f * ((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y));
+          const int s = c * kChunkSeqs + sub;
           if (s < n)
             *reinterpret_cast<uint16_t*>(sm + kOffSb + sw128_offset(s, feat, kGB)) =
                 to16<F16>(total);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&M.bar_free[bf]);
+          tc_fence_before();   // D2 reads ordered before the group's next MMA
         }
         fence_async_smem();                     // slot sums feed the W3 MMA
       }
