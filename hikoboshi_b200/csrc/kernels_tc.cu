@@ -547,25 +547,31 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           // would dominate), combined in a fixed order: slot i adds into
           // partial i mod 4, i.e. lane i mod 2 of pair (i mod 4) / 2.
           // Slots past K add an exact zero.
+          // (L >= 48, every full neighbourhood, takes the branch without the
+          // per-slot tests).
           float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-          auto sum_pairs = [&](const float* v, int n_pairs, int i0) {
+          auto sum_pairs = [&](const float* v, int n_pairs, int i0, bool full) {
 #pragma unroll
             for (int m = 0; m < n_pairs; ++m) {
               float2 gv = gelu2_tc_x2(__ffma2_rn(make_float2(v[2 * m], v[2 * m + 1]), half2c, b2p));
-              if (i0 + 2 * m >= K) gv.x = 0.0f;
-              if (i0 + 2 * m + 1 >= K) gv.y = 0.0f;
+              if (!full) {
+                if (i0 + 2 * m >= K) gv.x = 0.0f;
+                if (i0 + 2 * m + 1 >= K) gv.y = 0.0f;
+              }
               acc[m & 1] = __fadd2_rn(acc[m & 1], gv);
             }
           };
           {
             float v[32];
             tmem_ld32(tm + lane_base + d2col, v);
-            sum_pairs(v, 16, 0);
+            if (K == kK) sum_pairs(v, 16, 0, true);
+            else sum_pairs(v, 16, 0, false);
           }
           {
             float v[16];
             tmem_ld16(tm + lane_base + d2col + 32, v);
-            sum_pairs(v, 8, 32);
+            if (K == kK) sum_pairs(v, 8, 32, true);
+            else sum_pairs(v, 8, 32, false);
           }
           const float total = 0.5f * ((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y));
           const int s = c * kChunkSeqs + sub;
