@@ -401,12 +401,11 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           const int j = code & 0xFFFF;
           const bool bw = (code >> 16) & 1;
           const int64_t rt = M.off[s] + M.t[s];
-          pe_raw[i] = __ldg(reinterpret_cast<const uint4*>(PE + (rt * kK + k) * kH) + c8);
+          pe_raw[i] = ld_nc_noalloc_v4(PE + (rt * kK + k) * kH + c8 * 8);
           if (bw && layer > 0)   // written by this kernel: coherent load
-            v_raw[i] = reinterpret_cast<const uint4*>(PVl + (M.qrow[s] + j) * kH)[c8];
+            v_raw[i] = ld_noalloc_v4(PVl + (M.qrow[s] + j) * kH + c8 * 8);
           else
-            v_raw[i] =
-                __ldg(reinterpret_cast<const uint4*>(PVenc + (int64_t)(M.off[s] + j) * kH) + c8);
+            v_raw[i] = ld_nc_noalloc_v4(PVenc + (int64_t)(M.off[s] + j) * kH + c8 * 8);
         }
       }
     };

@@ -130,6 +130,26 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// 16-byte global loads that do not allocate in L1, for rows read once: they
+// would otherwise evict the small per-layer vectors that L1 keeps.  The .nc
+// form is for data that no thread writes during the kernel; the plain form
+// (ordered like any other memory access) for rows this kernel wrote.
+__device__ __forceinline__ uint4 ld_nc_noalloc_v4(const void* p) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_noalloc_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
 // Generic-proxy shared-memory writes become visible to the async proxy
 // (tensor cores, bulk copies).
 __device__ __forceinline__ void fence_async_smem() {
