@@ -41,17 +41,6 @@ using namespace tc;
 constexpr int kEncThreads = 512;
 constexpr uint32_t kW128Bytes = 128 * 128 * 2;   // one 128x128 fp16 weight image
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool pred) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
-               "r"(pred ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
 
 // GELU in its exact erf form with CUDA's erff.  The tensor-core path rounds
 // every result to fp16, so the reference's own erf approximation (A&S 7.1.26

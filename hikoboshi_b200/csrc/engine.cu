@@ -401,7 +401,8 @@ void append_gemm_image(std::vector<uint16_t>& img, const float* W, int ld, int r
     }
 }
 
-// All GEMM operands of the tensor-core encoder and decoder tables, by name.
+// The 16-bit GEMM operands of the fused tensor-core encoder kernels and the
+// decoder's PE tables, by name (the node-side GEMMs run in fp32).
 bool build_gemm_images(const std::map<std::string, TensorView>& t, std::vector<uint16_t>* img,
                        std::map<std::string, size_t>* at) {
   auto get = [&](const std::string& n) -> const float* {
@@ -422,31 +423,15 @@ bool build_gemm_images(const std::map<std::string, TensorView>& t, std::vector<u
     for (const char* nm : {"W1", "W11"}) {
       const float* W = get(p + nm + ".weight");
       if (!W) return false;
-      // [W1a ; W1c]: the h_i and h_j input blocks stacked as 256 output rows
-      std::vector<float> stack((size_t)256 * 128);
-      for (int r = 0; r < 128; ++r)
-        for (int k = 0; k < 128; ++k) {
-          stack[(size_t)r * 128 + k] = W[(size_t)r * 384 + k];
-          stack[(size_t)(128 + r) * 128 + k] = W[(size_t)r * 384 + 256 + k];
-        }
-      mark(q + nm + "ac");
-      append_gemm_image(*img, stack.data(), 128, 0, 256, 0, 128);
-      mark(q + nm + "b");
+      mark(q + nm + "b");   // the h_E input block
       append_gemm_image(*img, W, 384, 0, 128, 128, 128);
     }
-    for (const char* nm : {"W2", "W3", "W12", "W13"}) {
+    for (const char* nm : {"W2", "W12", "W13"}) {
       const float* W = get(p + nm + ".weight");
       if (!W) return false;
       mark(q + nm);
       append_gemm_image(*img, W, 128, 0, 128, 0, 128);
     }
-    const float* Wi = get(p + "dense.W_in.weight");
-    const float* Wo = get(p + "dense.W_out.weight");
-    if (!Wi || !Wo) return false;
-    mark(q + "Win");
-    append_gemm_image(*img, Wi, 128, 0, 512, 0, 128);
-    mark(q + "Wout");
-    append_gemm_image(*img, Wo, 512, 0, 128, 0, 512);
   }
   for (int l = 0; l < 3; ++l) {
     const std::string p = "decoder_layers." + std::to_string(l) + ".";
@@ -455,10 +440,6 @@ bool build_gemm_images(const std::map<std::string, TensorView>& t, std::vector<u
     if (!W1) return false;
     mark(q + "W1b");
     append_gemm_image(*img, W1, 512, 0, 128, 128, 128);
-    mark(q + "W1d");
-    append_gemm_image(*img, W1, 512, 0, 128, 384, 128);
-    mark(q + "W1a");
-    append_gemm_image(*img, W1, 512, 0, 128, 0, 128);
   }
   return true;
 }
@@ -726,22 +707,12 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
       !T3 || !h1 || !F || !Y)
     return {HKB_UNAVAILABLE, "device allocation failed"};
   const BatchView& bv = db.bv;
-  auto lin = [&](int64_t M, int N, int K, const void* A, int64_t lda, const char* img,
-                 const float* bias, int act, void* C, int64_t ldc, bool out_f16) {
-    LinearTcArgs p;
-    p.M = M;
-    p.N = N;
-    p.K = K;
-    p.A = A;
-    p.lda = lda;
-    p.W = e->gemm_img.at(img);
-    p.bias = bias;
-    p.act = act;
-    p.C = C;
-    p.ldc = ldc;
-    p.out_f16 = out_f16;
-    p.err = e->d_err;
-    launch_linear_tc(st, p, e->num_sms);
+  // Node-side GEMMs (M = R residue rows) in fp32 on the packed fp32 pipe:
+  // they are a small share of the encoder's work, and keeping them at fp32
+  // removes the largest 16-bit error source of the encoder.
+  auto lin = [&](int N, int K, const float* A, int lda, const float* WT, const float* bias,
+                 int act, float* C, int ldc) {
+    gemm_f32(st, R, N, K, A, lda, WT, N, bias, act, C, ldc);
     e->launches += 1;
   };
   launch_knn(st, bv, db.coords, db.sources, eo->e_idx, eo->d2, eo->mask, e->d_err, hb.max_len);
@@ -767,7 +738,7 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
     const auto& E = w.enc[l];
     const std::string q = "enc" + std::to_string(l) + ".";
     // node messages: one fused pass over h_E (W1b, gathers, GELU, W2, GELU, slot sum)
-    lin(R, 256, kH, eo->h_v, kH, (q + "W1ac").c_str(), E.b1ac, 0, NAC, 256, false);
+    lin(256, kH, eo->h_v, kH, E.W1acT, E.b1ac, 0, NAC, 256);
     EncNodeTcArgs na;
     na.bv = bv;
     na.h_e = eo->h_e16;
@@ -781,13 +752,13 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
     na.cnt = cnt;
     na.err = e->d_err;
     launch_enc_node_tc(st, na, e->num_sms);
-    lin(R, kH, kH, Sv, kH, (q + "W3").c_str(), nullptr, 0, T3, kH, false);
+    lin(kH, kH, Sv, kH, E.W3T, nullptr, 0, T3, kH);
     launch_enc_node_update(st, bv, T3, cnt, E.b3, eo->h_v, E.n1w, E.n1b, h1);
-    lin(R, kFfn, kH, h1, kH, (q + "Win").c_str(), E.bin, 1, F, kFfn, false);
-    lin(R, kH, kFfn, F, kFfn, (q + "Wout").c_str(), nullptr, 0, Y, kH, false);
+    lin(kFfn, kH, h1, kH, E.WinT, E.bin, 1, F, kFfn);
+    lin(kH, kFfn, F, kFfn, E.WoutT, nullptr, 0, Y, kH);
     launch_ln_rows(st, R, h1, Y, E.bout, E.n2w, E.n2b, eo->mask, nullptr, eo->h_v);
     // edge update: one fused pass (W11b, gathers, GELU, W12, GELU, W13, LN3)
-    lin(R, 256, kH, eo->h_v, kH, (q + "W11ac").c_str(), E.b11ac, 0, NAC, 256, false);
+    lin(256, kH, eo->h_v, kH, E.W11acT, E.b11ac, 0, NAC, 256);
     EncEdgeTcArgs ea;
     ea.bv = bv;
     ea.h_e = eo->h_e16;
@@ -826,23 +797,15 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const EncoderOu
     const std::string q = "dec" + std::to_string(l) + ".";
     ta.W[l] = e->gemm_img.at(q + "W1b");
     ta.out[l] = pe;
-    LinearTcArgs p;
-    p.N = kH;
-    p.K = kH;
-    p.err = e->d_err;
-    p.out_f16 = true;
-    p.M = R; p.A = eo.h_v; p.lda = kH; p.W = e->gemm_img.at(q + "W1d"); p.C = pv; p.ldc = kH;
-    launch_linear_tc(st, p, e->num_sms);
+    // W1d h_enc per residue, fp32 products rounded once to the 16-bit table
+    gemm_f32x2(st, R, kH, kH, eo.h_v, kH, e->w32.dec[l].W1dT, kH, nullptr, 0, pv, kH, true);
     tb->PE[l] = pe;
     tb->PVenc[l] = pv;
   }
   launch_dec_tables_tc(st, ta, e->num_sms);
   float* a0 = ws.get_as<float>("d.Aenc0", R * kH);
   if (!a0) return {HKB_UNAVAILABLE, "device allocation failed"};
-  LinearTcArgs p;
-  p.M = R; p.N = kH; p.K = kH; p.A = eo.h_v; p.lda = kH; p.W = e->gemm_img.at("dec0.W1a");
-  p.bias = e->w32.dec[0].b1; p.C = a0; p.ldc = kH; p.err = e->d_err;
-  launch_linear_tc(st, p, e->num_sms);
+  gemm_f32(st, R, kH, kH, eo.h_v, kH, e->w32.dec[0].W1aT, kH, e->w32.dec[0].b1, 0, a0, kH);
   tb->Aenc0 = a0;
   tb->h_enc = eo.h_v;
   e->launches += 5;

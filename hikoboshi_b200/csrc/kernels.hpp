@@ -75,6 +75,13 @@ struct DecoderTables {
 void gemm_f32(cudaStream_t st, int64_t M, int N, int K, const float* A, int lda,
               const float* B, int ldb, const float* bias, int act, float* C,
               int ldc);
+// The packed-fp32 tiled form gemm_f32 uses when the shape allows (N a
+// multiple of 128, K of 32, 16-byte aligned rows); out_f16 stores C as fp16.
+bool gemm_f32x2_fits(int N, int K, const void* A, int lda, const void* B, int ldb,
+                     const void* C, int ldc);
+void gemm_f32x2(cudaStream_t st, int64_t M, int N, int K, const float* A, int lda,
+                const float* B, int ldb, const float* bias, int act, void* C, int ldc,
+                bool out_f16);
 
 // Largest protein one call accepts (kNN keeps one 8-byte key per candidate
 // in shared memory and ranks every candidate against every other).
@@ -202,28 +209,6 @@ struct ArBf16Args {
   const int* e_idx;
   int64_t total_rows;
 };
-
-// Persistent tcgen05 GEMM C[M,N] = act(A[M,K] W[N,K]^T + bias): A fp32 or fp16
-// (row-major), W an fp16 SW128 image laid out [K/64 atoms][N rows x 64]
-// (K padded to a multiple of 64), fp32 accumulation in TMEM, output fp32 or
-// fp16.  N in {128, 256, 384, 512}, K <= 512.
-struct LinearTcArgs {
-  int64_t M = 0;
-  int N = 0;
-  int K = 0;
-  const void* A = nullptr;
-  int64_t lda = 0;
-  bool a_f16 = false;
-  const unsigned char* W = nullptr;
-  const float* bias = nullptr;
-  int act = 0;          // 0 none, 1 GELU (erf form)
-  void* C = nullptr;
-  int64_t ldc = 0;
-  bool out_f16 = false;
-  unsigned int* err = nullptr;
-};
-size_t linear_tc_smem_bytes(int N, int K);
-void launch_linear_tc(cudaStream_t st, const LinearTcArgs& p, int num_sms);
 
 // Fused encoder-layer kernels (tensor-core modes; h_E fp16 [R*48,128]).
 // NAC = [W1a h + b1 | W1c h] per residue, fp32 [R,256].

@@ -84,6 +84,125 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// fp32 GEMM on the packed fp32 pipe for N a multiple of 128 and K of 32:
+// C[M,N] = act(A[M,K] . B[K,N] + bias[N]).  128x128 output tile per
+// 256-thread block (two blocks per SM); thread (tx, ty) = (tid % 16,
+// tid / 16) owns rows 8 ty .. 8 ty + 7 and columns 8 tx .. 8 tx + 7, as
+// float2 column pairs updated by fma.rn.f32x2.  K advances 32 at a time
+// through two shared-memory stages filled by cp.async (the next slab loads
+// while the current one is multiplied); A stays row-major in shared memory
+// and a thread reads two consecutive k of each of its rows at once.  Each
+// output is one fp32 fma chain in k order (one rounding per term, as the
+// scalar kernel), then bias, then the activation.
+// ---------------------------------------------------------------------------
+constexpr int kG2Tile = 128;
+constexpr int kG2K = 32;
+constexpr int kG2APitch = kG2K + 4;   // floats per As row: 144 B, 16-byte aligned
+constexpr size_t kG2Smem = (size_t)2 * (kG2Tile * kG2APitch + kG2K * kG2Tile) * sizeof(float);
+
+template <int ACT, bool OUT16>
+__global__ void __launch_bounds__(256, 2) gemm_f32x2_kernel(
+    int64_t M, int K, const float* __restrict__ A, int lda, const float* __restrict__ B, int ldb,
+    const float* __restrict__ bias, void* __restrict__ C, int ldc) {
+  extern __shared__ __align__(16) float g2_smem[];
+  float (*As)[kG2Tile][kG2APitch] = reinterpret_cast<float (*)[kG2Tile][kG2APitch]>(g2_smem);
+  float (*Bs)[kG2K][kG2Tile] =
+      reinterpret_cast<float (*)[kG2K][kG2Tile]>(g2_smem + 2 * kG2Tile * kG2APitch);
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = (int64_t)blockIdx.x * kG2Tile;
+  const int n0 = blockIdx.y * kG2Tile;
+  // One slab: A 128 rows x 32 k and B 32 rows x 128 n, 1024 16-byte chunks
+  // each.  Thread chunk q (0..3) of A is row tid / 8 + 32 q, k 4 (tid % 8);
+  // of B row tid / 32 + 8 q, n 4 (tid % 32).  Rows of A past M are
+  // zero-filled.
+  const int ar = tid >> 3, ak = (tid & 7) * 4;
+  const int bk = tid >> 5, bn = (tid & 31) * 4;
+  const float* a_base = A + (m0 + ar) * lda + ak;
+  const float* b_base = B + (int64_t)bk * ldb + n0 + bn;
+  auto load = [&](int k0, int stage) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const bool ok = m0 + ar + 32 * q < M;
+      cp_async16(&As[stage][ar + 32 * q][ak], ok ? a_base + (int64_t)(32 * q) * lda + k0 : A, ok);
+      cp_async16(&Bs[stage][bk + 8 * q][bn], b_base + (int64_t)(k0 + 8 * q) * ldb, true);
+    }
+    cp_async_commit();
+  };
+  float2 acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
+
+  const int slabs = K / kG2K;
+  load(0, 0);
+  for (int t = 0; t < slabs; ++t) {
+    const int cur = t & 1;
+    if (t + 1 < slabs) {
+      load((t + 1) * kG2K, cur ^ 1);
+      cp_async_wait_one();
+    } else {
+      cp_async_wait_all();
+    }
+    __syncthreads();
+#pragma unroll 1   // (full unrolling hoists the next step's loads and spills)
+    for (int k2 = 0; k2 < kG2K; k2 += 2) {
+      float2 a2[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a2[i] = *reinterpret_cast<const float2*>(&As[cur][ty * 8 + i][k2]);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][k2 + u][tx * 8]);
+        const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][k2 + u][tx * 8 + 4]);
+        const float2 bv[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
+                              make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float a = u == 0 ? a2[i].x : a2[i].y;
+          const float2 ai = make_float2(a, a);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = __ffma2_rn(ai, bv[j], acc[i][j]);
+        }
+      }
+    }
+    __syncthreads();   // stage cur is refilled by the next iteration's load
+  }
+  float bb[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) bb[j] = bias ? bias[n0 + tx * 8 + j] : 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t gm = m0 + ty * 8 + i;
+    if (gm >= M) continue;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = acc[i][j].x + bb[2 * j];
+      v[2 * j + 1] = acc[i][j].y + bb[2 * j + 1];
+    }
+    if (ACT == 1) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = gelu_as(v[j]);
+    }
+    if constexpr (OUT16) {
+      uint32_t h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __half2 p = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+        h[j] = *reinterpret_cast<const uint32_t*>(&p);
+      }
+      *reinterpret_cast<uint4*>(static_cast<__half*>(C) + gm * ldc + n0 + tx * 8) =
+          make_uint4(h[0], h[1], h[2], h[3]);
+    } else {
+      float* c = static_cast<float*>(C) + gm * ldc + n0 + tx * 8;
+      *reinterpret_cast<float4*>(c) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(c + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // CA kNN, one block per query residue.  Reference semantics
 // (cpp/primitives/compute/knn_scalar.cpp:72-168 as configured by
 // cpp/modules/mpnn/inverse_fold_scalar.cpp:211-234): d^2 = dx^2 + dy^2 + dz^2
@@ -800,11 +919,52 @@ void gemm_f32(cudaStream_t st, int64_t M, int N, int K, const float* A, int lda,
               const float* B, int ldb, const float* bias, int act, float* C,
               int ldc) {
   if (M <= 0) return;
+  if (gemm_f32x2_fits(N, K, A, lda, B, ldb, C, ldc)) {
+    gemm_f32x2(st, M, N, K, A, lda, B, ldb, bias, act, C, ldc, false);
+    return;
+  }
   dim3 grid((unsigned)((M + 63) / 64), (N + 63) / 64);
   if (act == 1)
     gemm_f32_kernel<1><<<grid, 256, 0, st>>>(M, N, K, A, lda, B, ldb, bias, C, ldc);
   else
     gemm_f32_kernel<0><<<grid, 256, 0, st>>>(M, N, K, A, lda, B, ldb, bias, C, ldc);
+}
+
+bool gemm_f32x2_fits(int N, int K, const void* A, int lda, const void* B, int ldb,
+                     const void* C, int ldc) {
+  auto al16 = [](const void* p) { return ((uintptr_t)p & 15u) == 0; };
+  return N > 0 && N % kG2Tile == 0 && K > 0 && K % kG2K == 0 && lda % 4 == 0 &&
+         ldb % 4 == 0 && ldc % 8 == 0 && al16(A) && al16(B) && al16(C);
+}
+
+void gemm_f32x2(cudaStream_t st, int64_t M, int N, int K, const float* A, int lda,
+                const float* B, int ldb, const float* bias, int act, void* C, int ldc,
+                bool out_f16) {
+  if (M <= 0) return;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm_f32x2_kernel<0, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kG2Smem);
+    cudaFuncSetAttribute(gemm_f32x2_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kG2Smem);
+    cudaFuncSetAttribute(gemm_f32x2_kernel<0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kG2Smem);
+    cudaFuncSetAttribute(gemm_f32x2_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kG2Smem);
+    attr_set = true;
+  }
+  const dim3 grid((unsigned)((M + kG2Tile - 1) / kG2Tile), N / kG2Tile);
+  if (out_f16) {
+    if (act == 1)
+      gemm_f32x2_kernel<1, true><<<grid, 256, kG2Smem, st>>>(M, K, A, lda, B, ldb, bias, C, ldc);
+    else
+      gemm_f32x2_kernel<0, true><<<grid, 256, kG2Smem, st>>>(M, K, A, lda, B, ldb, bias, C, ldc);
+  } else {
+    if (act == 1)
+      gemm_f32x2_kernel<1, false><<<grid, 256, kG2Smem, st>>>(M, K, A, lda, B, ldb, bias, C, ldc);
+    else
+      gemm_f32x2_kernel<0, false><<<grid, 256, kG2Smem, st>>>(M, K, A, lda, B, ldb, bias, C, ldc);
+  }
 }
 
 void launch_knn(cudaStream_t st, const BatchView& bv, const float* coords,

@@ -117,10 +117,11 @@ def test_f16_config3_long_chain(engine_f16, engine_fp32, oracle):
     kNN over 1024 CA, a [1024,48,128] edge tensor and a 1024-step decode over
     128 two-sequence groups.
 
-    Tolerance 3e-2, not the 2e-2 16-bit bar: on this long chain the fp16
-    engine's maximum log-prob error is 0.023-0.028 (fp16 weights and operands
-    throughout; config 2 stays at 0.015-0.017).  The fp32 mode meets 1e-4 here
-    (test_fp32_config3_long_chain_matches_oracle)."""
+    Tolerance 2.5e-2, not the 2e-2 16-bit bar: on this long chain the fp16
+    engine's maximum log-prob error is 0.022 (fp16 weights and operands in
+    the edge-wise encoder and the decoder; config 2 stays at 0.010-0.016).
+    The engine is deterministic, so the figure repeats exactly.  The fp32 mode
+    meets 1e-4 here (test_fp32_config3_long_chain_matches_oracle)."""
     from hikoboshi_b200 import decode_order, synthetic_backbone
     c, s = synthetic_backbone(11, 1024)
     res = engine_f16.design([c], [s], num_seqs=256, seeds=0, temperatures=0.2)
@@ -130,7 +131,7 @@ def test_f16_config3_long_chain(engine_f16, engine_fp32, oracle):
     assert np.abs(lse).max() < 1e-4
     for q in (0, 255):
         assert (orders[q] == decode_order(1024, q)).all()
-    _check_vs_fp32_tf(engine_fp32, oracle, c, s, tok, lp, orders, 0, 0.2, [0, 97, 255], 3e-2)
+    _check_vs_fp32_tf(engine_fp32, oracle, c, s, tok, lp, orders, 0, 0.2, [0, 97, 255], 2.5e-2)
 
 
 def test_f16_config5_mixed_lengths(engine_f16, engine_fp32, oracle):
