@@ -42,13 +42,10 @@ constexpr int kEncThreads = 512;
 constexpr uint32_t kW128Bytes = 128 * 128 * 2;   // one 128x128 fp16 weight image
 
 
-// GELU in its exact erf form with CUDA's erff.  The tensor-core path rounds
-// every result to fp16, so the reference's own erf approximation (A&S 7.1.26
-// with a table-driven exp, kept by the fp32 parity path) buys nothing here
-// and costs a division and per-lane constant-table lookups.
-__device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-}
+// The GELUs here use the fitted tanh form (gelu_tc_x2, max error 2.5e-5)
+// on the packed fp32 pipe: every result is rounded to fp16 (4.9e-4 relative)
+// or summed with other fitted values, so the exact erf form would buy nothing
+// at several times the instructions.
 
 // RBF value f of 16 for the fp16 feature operand: exp(-((d - c_f) / 1.25)^2)
 // with c_f = 2 + f * 20/15 and 2 sigma^2 = 1.5625 (the reference's centres and
@@ -199,12 +196,16 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       float v[16];
       tmem_ld16(tm + lane_base + (uint32_t)(rho * kK + k0), v);
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
+      for (int k = 0; k < 16; k += 2) {
         const int c = rho * kK + k0 + k;
-        const int rj = SJ[c];
-        const float nc = rj >= 0 ? p.NAC[(int64_t)rj * 256 + 128 + f] : 0.0f;
-        const float y = rj >= 0 ? gelu_erf(v[k] + na + nc) : 0.0f;
-        *reinterpret_cast<__half*>(G + sw128_offset(c, f, kNodeSlots)) = __float2half_rn(y);
+        const int rj0 = SJ[c], rj1 = SJ[c + 1];
+        const float nc0 = rj0 >= 0 ? p.NAC[(int64_t)rj0 * 256 + 128 + f] : 0.0f;
+        const float nc1 = rj1 >= 0 ? p.NAC[(int64_t)rj1 * 256 + 128 + f] : 0.0f;
+        const float2 y = gelu_tc_x2(make_float2(v[k] + na + nc0, v[k + 1] + na + nc1));
+        *reinterpret_cast<__half*>(G + sw128_offset(c, f, kNodeSlots)) =
+            __float2half_rn(rj0 >= 0 ? y.x : 0.0f);
+        *reinterpret_cast<__half*>(G + sw128_offset(c + 1, f, kNodeSlots)) =
+            __float2half_rn(rj1 >= 0 ? y.y : 0.0f);
       }
     }
     fence_async_smem();
@@ -222,20 +223,27 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     // epilogue 2: masked slot sum of GELU(D2 + b2): four interleaved partial
     // sums (slot k goes to k % 4) combined in a fixed order
     {
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cnt = 0.0f;
+      // (partials 0,1 and 2,3 as float2 pairs: slots k, k+1 with k % 4 = 0
+      // go to pair 0, with k % 4 = 2 to pair 1; a * GELU(x) is one fma of
+      // a/2 and twice the GELU, exact scalings by 2)
+      float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+      float cnt = 0.0f;
+      const float2 b2p = make_float2(b2, b2);
 #pragma unroll 1
       for (int k0 = 0; k0 < kK; k0 += 16) {
         float v[16];
         tmem_ld16(tm + lane_base + (uint32_t)(rho * kK + k0), v);
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float a = SA[rho * kK + k0 + k];
-          acc[k & 3] += a * gelu_erf(v[k] + b2);
-          cnt += a;
+        for (int k = 0; k < 16; k += 2) {
+          const float a0 = SA[rho * kK + k0 + k], a1 = SA[rho * kK + k0 + k + 1];
+          const float2 g2 = gelu2_tc_x2(__fadd2_rn(make_float2(v[k], v[k + 1]), b2p));
+          acc[(k >> 1) & 1] = __ffma2_rn(make_float2(0.5f * a0, 0.5f * a1), g2, acc[(k >> 1) & 1]);
+          cnt += a0;
+          cnt += a1;
         }
       }
       if (r < R) {
-        p.S[(int64_t)r * kH + f] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        p.S[(int64_t)r * kH + f] = (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
         if (f == 0) p.cnt[r] = cnt;
       }
     }
@@ -343,12 +351,12 @@ __global__ void __launch_bounds__(kEncThreads, 1)
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const float4 a = na[q], c = nc[q];
-          const float y0 = gelu_erf(v[4 * q + 0] + a.x + c.x);
-          const float y1 = gelu_erf(v[4 * q + 1] + a.y + c.y);
-          const float y2 = gelu_erf(v[4 * q + 2] + a.z + c.z);
-          const float y3 = gelu_erf(v[4 * q + 3] + a.w + c.w);
-          pk[2 * q] = pack_h2(y0, y1);
-          pk[2 * q + 1] = pack_h2(y2, y3);
+          const float2 y01 = gelu_tc_x2(make_float2(v[4 * q + 0] + a.x + c.x,
+                                                    v[4 * q + 1] + a.y + c.y));
+          const float2 y23 = gelu_tc_x2(make_float2(v[4 * q + 2] + a.z + c.z,
+                                                    v[4 * q + 3] + a.w + c.w));
+          pk[2 * q] = pack_h2(y01.x, y01.y);
+          pk[2 * q + 1] = pack_h2(y23.x, y23.y);
         }
       } else {
 #pragma unroll
@@ -376,9 +384,11 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       tmem_ld32(tm + lane_base + 128u + (uint32_t)c0, v);
       uint32_t pk[16];
 #pragma unroll
-      for (int q = 0; q < 16; ++q)
-        pk[q] = pack_h2(gelu_erf(v[2 * q] + p.b12[c0 + 2 * q]),
-                        gelu_erf(v[2 * q + 1] + p.b12[c0 + 2 * q + 1]));
+      for (int q = 0; q < 16; ++q) {
+        const float2 y = gelu_tc_x2(make_float2(v[2 * q] + p.b12[c0 + 2 * q],
+                                                v[2 * q + 1] + p.b12[c0 + 2 * q + 1]));
+        pk[q] = pack_h2(y.x, y.y);
+      }
 #pragma unroll
       for (int u = 0; u < 4; ++u)
         *reinterpret_cast<uint4*>(G + sw128_offset(row, c0 + 8 * u, 128)) =
