@@ -153,11 +153,14 @@ __device__ __forceinline__ unsigned long long splitmix_next(unsigned long long& 
   return z ^ (z >> 31);
 }
 
-// Thread-0 state of the weight-tile stream.
+// Thread-0 state of the weight-tile stream.  32-bit counters (at most
+// 4096 x 34 tiles): the slot and tile indices are taken modulo 3 and 34 on
+// every issue, on thread 0's critical path, and 64-bit remainders cost
+// several times more.
 struct Stream {
-  long long issued;   // tiles whose loads were issued
-  long long used;     // tiles whose last MMA was issued
-  long long total;    // tiles this CTA consumes
+  int issued;   // tiles whose loads were issued
+  int used;     // tiles released (their MMAs complete)
+  int total;    // tiles this CTA consumes
 };
 
 __device__ __forceinline__ void stream_issue(Stream& s, unsigned char* sm, Misc& M,
@@ -165,8 +168,8 @@ __device__ __forceinline__ void stream_issue(Stream& s, unsigned char* sm, Misc&
   // Issue loads while a slot is free: tile j may load once tile j - kSlots is
   // released (its MMAs complete, tracked by `used` after a commit wait).
   while (s.issued < s.total && s.issued < s.used + kSlots) {
-    const int slot = (int)(s.issued % kSlots);
-    const int tile = (int)(s.issued % kStreamTilesPerStep);
+    const int slot = s.issued % kSlots;
+    const int tile = s.issued % kStreamTilesPerStep;
     mbar_arrive_expect_tx(&M.full[slot], kTileBytes);
     bulk_g2s(sm + kOffW + slot * kTileBytes, img + (size_t)tile * kTileBytes, kTileBytes,
              &M.full[slot]);
@@ -175,9 +178,9 @@ __device__ __forceinline__ void stream_issue(Stream& s, unsigned char* sm, Misc&
 }
 
 // Waits until tile `j` is resident; returns its shared address.
-__device__ __forceinline__ uint32_t stream_wait(long long j, unsigned char* sm, Misc& M,
+__device__ __forceinline__ uint32_t stream_wait(int j, unsigned char* sm, Misc& M,
                                                 unsigned int* err) {
-  const int slot = (int)(j % kSlots);
+  const int slot = j % kSlots;
   if (!mbar_wait(&M.full[slot], (uint32_t)((j / kSlots) & 1), err))
     *reinterpret_cast<volatile int*>(&M.abort_flag) = 1;
   return smem_u32(sm + kOffW + slot * kTileBytes);
@@ -251,7 +254,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   tc_fence_after();
   const uint32_t tm = M.tbase;   // TMEM base address
 
-  Stream st{0, 0, (long long)L * kStreamTilesPerStep};
+  Stream st{0, 0, L * kStreamTilesPerStep};
   if (tid == 0) stream_issue(st, sm, M, w.stream);
 
   // decode positions of every residue of this CTA's sequences
@@ -275,7 +278,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   uint4 raw_pe[kRowsPerThread], raw_v[kRowsPerThread];   // in-flight slot rows
   uint32_t d2_count = 0;   // this group's message MMAs waited for so far
   uint32_t ph_all = 0;
-  long long tile = 0;   // next tile to consume (same on all threads)
+  int tile = 0;   // next tile to consume (same on all threads)
 
   for (int p = 0; p < L; ++p) {
     // uniform exit: every thread takes the same branch
@@ -778,8 +781,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   }
   // Drain: no bulk copy may still be in flight when the CTA exits.
   if (tid == 0) {
-    for (long long j = tile; j < st.issued; ++j) {
-      const int slot = (int)(j % kSlots);
+    for (int j = tile; j < st.issued; ++j) {
+      const int slot = j % kSlots;
       mbar_wait(&M.full[slot], (uint32_t)((j / kSlots) & 1), err);
     }
   }
