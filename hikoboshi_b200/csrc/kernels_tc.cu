@@ -431,6 +431,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       if (__syncthreads_or(M.abort_flag)) break;
       // ---- node terms for l >= 1 (MMAs issued at the end of layer l-1) -----
       if (l > 0) {
+        const float b1 = w.b1[l][feat];        // in flight during the wait
         if (!mbar_wait(&M.bar_all, ph_all, err)) *abort_p = 1;
         ph_all ^= 1;
         tc_fence_after();
@@ -443,7 +444,6 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         const int s0 = (wg & 1) * 8;
         if (wg < 2) {
           tmem_ld8(tm + lane_base + kColA + s0, v);
-          const float b1 = w.b1[l][feat];
 #pragma unroll
           for (int q = 0; q < 8; ++q) Aa[s0 + q][feat] = v[q] + b1;
         } else {
@@ -552,6 +552,12 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       ++tile;                                   // W2 consumed
       __syncthreads();
       // ---- W3 after the slot sum, residual + LayerNorm 1 --------------------
+      // This layer's epilogue biases, loaded while the W3 MMA runs (a load
+      // issued after an MMA wait would put its latency on the critical path).
+      const float b3 = w.b3[l][feat] * (float)K;
+      const float b_in0 = w.bin[l][feat], b_in1 = w.bin[l][128 + feat];
+      const float b_in2 = w.bin[l][256 + feat], b_in3 = w.bin[l][384 + feat];
+      const float b_out = w.bout[l][feat];
       if (tid == 0) {
         st.used = tile;                         // W2's MMAs have completed
         stream_issue(st, sm, M, w.stream);
@@ -572,7 +578,6 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       {
         float v[4];
         tmem_ld4(tm + lane_base + kColD3 + wg * 4, v);
-        const float b3 = w.b3[l][feat] * (float)K;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int s = wg * 4 + q;
@@ -642,7 +647,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         {
           float v[4];
           tmem_ld4(tm + lane_base + kColDF + wg * 4, v);
-          const float bi = w.bin[l][i * 128 + feat];
+          const float bi = i == 0 ? b_in0 : i == 1 ? b_in1 : i == 2 ? b_in2 : b_in3;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int s = wg * 4 + q;
@@ -673,7 +678,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       {
         float v[4];
         tmem_ld4(tm + lane_base + kColDO + wg * 4, v);
-        const float bo = w.bout[l][feat];
+        const float bo = b_out;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int s = wg * 4 + q;
