@@ -202,15 +202,19 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 }
 
 // K = 128 product of one 128-row A tile and an N-row B tile (both SW128
-// K-major, 2 atoms along K), accumulating into D when `acc` is set.
+// K-major, 2 atoms along K), accumulating into D when `acc` is set.  The
+// descriptor's start-address field (address >> 4, 14 bits) is linear in the
+// address and shared memory lies below 256 KB, so step kk's descriptors are
+// the tile's base descriptors plus (offset >> 4): no field can carry.
 __device__ __forceinline__ void mma_k128(uint32_t d_tmem, uint32_t a_smem, uint32_t b_smem,
                                          int n_rows, uint32_t idesc, bool acc) {
+  const uint64_t da = sw128_desc(a_smem), db = sw128_desc(b_smem);
+  const uint64_t b_atom = (uint64_t)((uint32_t)n_rows * 128u >> 4);
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
-    const uint32_t off = (uint32_t)((kk & 3) * 32);
-    const uint32_t a = a_smem + (uint32_t)(kk >> 2) * 128u * 128u + off;
-    const uint32_t b = b_smem + (uint32_t)(kk >> 2) * (uint32_t)n_rows * 128u + off;
-    mma_bf16(d_tmem, sw128_desc(a), sw128_desc(b), idesc, (acc || kk > 0) ? 1u : 0u);
+    const uint64_t off = (uint64_t)((kk & 3) * 2);   // 32 bytes >> 4
+    mma_bf16(d_tmem, da + (uint64_t)(kk >> 2) * (128u * 128u >> 4) + off,
+             db + (uint64_t)(kk >> 2) * b_atom + off, idesc, (acc || kk > 0) ? 1u : 0u);
   }
 }
 
