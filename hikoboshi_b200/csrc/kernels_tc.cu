@@ -68,8 +68,12 @@ constexpr uint32_t kOffXs = kOffAa + kGB * kH * 4;
 constexpr uint32_t kOffNb = kOffXs + kGB * kH * 4;              // int [16,48]
 constexpr uint32_t kOffLogit = kOffNb + kGB * kK * 4;           // float [16,32]
 constexpr uint32_t kOffStab = kOffLogit + kGB * 32 * 4;         // 16-bit [3,21,128]
-constexpr uint32_t kOffHead = kOffStab + 16384;                 // fp32 [128,21]
-constexpr uint32_t kOffNbNext = kOffHead + kH * kV * 4;        // int [16,48] next position
+constexpr uint32_t kOffHead = kOffStab + 16384;                 // fp32 [21][kHeadPitch]
+// Logit head stored transposed, one padded row per vocabulary entry: a logit
+// is a float4 walk along both operands, and the 528-byte pitch spreads eight
+// consecutive entries over all 32 banks.
+constexpr int kHeadPitch = kH + 4;
+constexpr uint32_t kOffNbNext = kOffHead + kV * kHeadPitch * 4; // int [16,48] next position
 constexpr uint32_t kOffMisc = kOffNbNext + kGB * kK * 4;
 constexpr uint32_t kSmemBytes = kOffMisc + 1024 + 1024;         // + misc + alignment slack
 
@@ -244,7 +248,10 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     const int l = e / (kV * kH), r = e % (kV * kH);
     StabS[e] = to16<F16>(w.Stab[l][r]);
   }
-  for (int e = tid; e < kH * kV; e += kThreadsB) HeadS[e] = w.headT[e];
+  for (int e = tid; e < kH * kV; e += kThreadsB) {
+    const int v = e / kH, f = e % kH;
+    HeadS[v * kHeadPitch + f] = w.headT[f * kV + v];
+  }
   if (warp == 0) {
     tmem_alloc(&M.tbase, kTmemCols);
     tmem_relinquish();
@@ -727,8 +734,16 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       float z = 0.0f;
       if (s < n) {
         z = w.head_b[v];
+        const float4* hr = reinterpret_cast<const float4*>(hS[s]);
+        const float4* wr = reinterpret_cast<const float4*>(HeadS + v * kHeadPitch);
 #pragma unroll 8
-        for (int f = 0; f < kH; ++f) z = fmaf(hS[s][f], HeadS[f * kV + v], z);
+        for (int f4 = 0; f4 < kH / 4; ++f4) {   // same fma order as f = 0..127
+          const float4 h = hr[f4], wv = wr[f4];
+          z = fmaf(h.x, wv.x, z);
+          z = fmaf(h.y, wv.y, z);
+          z = fmaf(h.z, wv.z, z);
+          z = fmaf(h.w, wv.w, z);
+        }
       }
       Lg[s][v] = z;
     }
