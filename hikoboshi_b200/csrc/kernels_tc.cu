@@ -287,6 +287,17 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   uint32_t ph_all = 0;
   int tile = 0;   // next tile to consume (same on all threads)
 
+  // The next position's h_enc / Aenc0 rows (residue t_next of each sequence)
+  // into a free [16,128] fp32 buffer by cp.async: 16 rows x 32 16-byte chunks,
+  // one per thread; absent sequences are zero-filled.
+  auto stage_next_rows = [&](float (*dst)[kH], const float* table) {
+    const int s = tid >> 5, c = tid & 31;
+    const bool live = s < n;
+    const float* src = live ? table + (int64_t)(M.off[s] + M.t_next[s]) * kH + c * 4 : table;
+    cp_async16(&dst[s][c * 4], src, live);
+    cp_async_commit();
+  };
+
   for (int p = 0; p < L; ++p) {
     // uniform exit: every thread takes the same branch
     if (__syncthreads_or(M.abort_flag)) break;
@@ -335,10 +346,14 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       }
       __syncthreads();
     }
-    for (int e = tid; e < kGB * kH; e += kThreadsB) {
-      const int s = e >> 7, f = e & 127;
-      hS[s][f] = s < n ? tb.h_enc[(int64_t)(M.off[s] + M.t[s]) * kH + f] : 0.0f;
-      Aa[s][f] = s < n ? tb.Aenc0[(int64_t)(M.off[s] + M.t[s]) * kH + f] : 0.0f;
+    if (p == 0) {
+      for (int e = tid; e < kGB * kH; e += kThreadsB) {
+        const int s = e >> 7, f = e & 127;
+        hS[s][f] = s < n ? tb.h_enc[(int64_t)(M.off[s] + M.t[s]) * kH + f] : 0.0f;
+        Aa[s][f] = s < n ? tb.Aenc0[(int64_t)(M.off[s] + M.t[s]) * kH + f] : 0.0f;
+      }
+    } else {
+      cp_async_wait_all();   // rows staged during the previous position's logits
     }
     // the next position's residue and mask, for the prefetch in layer 2
     if (tid < kGB) {
@@ -728,6 +743,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       }
     }
     if (__syncthreads_or(M.abort_flag)) break;
+    // Aa is free from here to the next position's set-up
+    if (p + 1 < L) stage_next_rows(Aa, tb.Aenc0);
     // ---- logits and sampling ------------------------------------------------
     for (int e = tid; e < kGB * kV; e += kThreadsB) {
       const int s = e / kV, v = e % kV;
@@ -748,6 +765,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       Lg[s][v] = z;
     }
     __syncthreads();
+    if (p + 1 < L) stage_next_rows(hS, tb.h_enc);   // hS is no longer read
     // One warp per sequence, one lane per vocabulary entry
     // (sampler_scalar.cpp:49-92): temperature-scaled log-softmax emitted as
     // the log-prob row, then greedy argmax (first maximum) or one uniform draw
@@ -799,6 +817,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     }
     __syncthreads();
   }
+  cp_async_wait_all();   // staged rows of a position an abort skipped
   // Drain: no bulk copy may still be in flight when the CTA exits.
   if (tid == 0) {
     for (int j = tile; j < st.issued; ++j) {
