@@ -187,18 +187,20 @@ __device__ __forceinline__ float warp_max(float v) {
 // two-pass mean / population variance, eps 1e-5 (reference semantics:
 // cpp/primitives/compute/layer_norm_scalar.cpp:8-40 computes the same
 // statistics with Welford's update).
+// g and b are 16-byte aligned rows of 128 (every weight row is).
 __device__ __forceinline__ void warp_layer_norm128(float (&x)[4], const float* g,
                                                   const float* b, int lane) {
+  const float4 gv = reinterpret_cast<const float4*>(g)[lane];   // in flight during the sums
+  const float4 bv = reinterpret_cast<const float4*>(b)[lane];
   float s = warp_sum(x[0] + x[1] + x[2] + x[3]);
   const float mean = s * (1.0f / 128.0f);
   float d0 = x[0] - mean, d1 = x[1] - mean, d2 = x[2] - mean, d3 = x[3] - mean;
   float v = warp_sum(d0 * d0 + d1 * d1 + d2 * d2 + d3 * d3) * (1.0f / 128.0f);
   const float inv = 1.0f / sqrtf(v + kLnEps);
-  const int c = lane * 4;
-  x[0] = d0 * inv * g[c + 0] + b[c + 0];
-  x[1] = d1 * inv * g[c + 1] + b[c + 1];
-  x[2] = d2 * inv * g[c + 2] + b[c + 2];
-  x[3] = d3 * inv * g[c + 3] + b[c + 3];
+  x[0] = d0 * inv * gv.x + bv.x;
+  x[1] = d1 * inv * gv.y + bv.y;
+  x[2] = d2 * inv * gv.z + bv.z;
+  x[3] = d3 * inv * gv.w + bv.w;
 }
 
 }  // namespace hkb

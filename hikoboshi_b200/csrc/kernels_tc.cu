@@ -581,13 +581,15 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       const float b_in2 = w.bin[l][256 + feat], b_in3 = w.bin[l][384 + feat];
       const float b_out = w.bout[l][feat];
       if (tid == 0) {
-        st.used = tile;                         // W2's MMAs have completed
-        stream_issue(st, sm, M, w.stream);
         const uint32_t wa = stream_wait(tile, sm, M, err);
         tc_fence_after();
         if (!*abort_p)
           mma_k128(tm + kColD3, wa, smem_u32(sm + kOffSb), kGB, idesc16<F16>(128, kGB), false);
         mma_commit(&M.bar_all);
+        // W2's MMAs have completed; its slot's next tile is not needed before
+        // the FFN, so the refill follows the W3 MMA instead of delaying it
+        st.used = tile;
+        stream_issue(st, sm, M, w.stream);
       }
       ++tile;                                   // W3
       if (!mbar_wait(&M.bar_all, ph_all, err)) *abort_p = 1;
