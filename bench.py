@@ -7,13 +7,16 @@ per sequence: featurisation, encoder, decoder tables and the autoregressive
 decode of all 2,048 sequences (524,288 designed residues per GPU).
 
 * ``value``  -- inputs resident in HBM (hkb_mpnn_design_device); per-step
-  device time from CUDA events on the launching stream (host-side order
-  generation inside the interval); L2 flushed (512 MiB write) before each step.
+  device time from CUDA events on the launching stream (the decoding orders
+  are generated on the device inside the interval); L2 flushed (512 MiB
+  write) before each step.
 * ``e2e``    -- the host API (hkb_mpnn_design): pinned coords/atom-sources
   uploaded and tokens + log-probs + scores read back every step; wall clock.
 * ``roofline`` -- the autoregressive decode kernel (the dominant kernel):
   algorithmic FLOPs per launch (29,103,360 per designed residue, the reference
-  formulation) over its CUDA-event duration, against MEASURED_PEAKS.json.
+  formulation) over its CUDA-event duration, against the measured burst 16-bit
+  tensor peak of MEASURED_PEAKS.json (the kernel is timed on its own, within a
+  step of a few tens of milliseconds).
 * ``cpu_baseline`` -- the reference's own CPU design path (oracle/_ref, the
   reference sources compiled here) on the host cores, bounded sample.
 
@@ -190,11 +193,12 @@ def cpu_baseline_sample(threads: int, seqs_per_thread: int = 1):
     `seqs_per_thread` sequences of its own config-2 backbone (L=256, T=0.1,
     random order).  Returns (residues/s, description)."""
     from concurrent.futures import ThreadPoolExecutor
-    from hikoboshi_b200 import synthetic_backbone
     from oracle.oracle import RefLib
 
+    # The inputs come from the generator linked into the reference library,
+    # so this leg never loads the engine library.
     ref = RefLib(WEIGHTS)
-    inputs = [synthetic_backbone(i % N_PROT, L_RES) for i in range(threads)]
+    inputs = [ref.synthetic_backbone(i % N_PROT, L_RES) for i in range(threads)]
 
     def one(i):
         c, s = inputs[i]
@@ -366,7 +370,7 @@ def run_ours(args):
         res_step = Q * world
         value = res_step / step_s
         peaks, kind = measured_peaks()
-        peak = peaks["bf16_tflops_sustained"] if args.precision != "fp32" else peaks["bf16_tflops"]
+        peak = peaks["bf16_tflops"]
         achieved = FLOP_DECODE_PER_RES * Q / dec_s / 1e12
         traffic = profiled_traffic(args.precision)
         line = {
@@ -387,8 +391,7 @@ def run_ours(args):
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "flops_per_launch": FLOP_DECODE_PER_RES * Q,
-                         "peak_kind": f"{kind} dense 16-bit tensor "
-                                      f"{'sustained' if args.precision != 'fp32' else 'burst'}"},
+                         "peak_kind": f"{kind} dense 16-bit tensor burst"},
             "e2e": {"value": res_step / e2e_s, "unit": "residues/s",
                     "h2d_bytes_per_step": int(coords_h.nbytes + src_h.nbytes),
                     "d2h_bytes_per_step": int(Q * 4 + Q * 21 * 4 + NS * 4)},

@@ -22,7 +22,7 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU_SOURCES = ["kernels_f32.cu", "kernels_tc.cu", "enc_tc.cu", "engine.cu",
+CU_SOURCES = ["kernels_f32.cu", "kernels_tc.cu", "enc_tc.cu", "orders.cu", "engine.cu",
               "noalloc.cu"]
 CPP_SOURCES = ["host_order.cpp", "host_synth.cpp", "safetensors.cpp", "structure_io.cpp",
                "host_io.cpp"]
@@ -92,7 +92,14 @@ WEIGHTS_NAME = "Hikoboshi-ProteinMPNN-v48-020.safetensors"
 WEIGHTS_SHA256 = "342b52ae248f2b70b2059313bab5ae7a358cbabac940072f71f5907eeaa21536"
 
 
-def stage_weights(reference_root: str = "/root/reference") -> Path:
+def reference_root() -> Path:
+    """The reference checkout: $HKB_REFERENCE_ROOT if set, else a checkout
+    named ``reference`` beside this repository (it may be absent)."""
+    env = os.environ.get("HKB_REFERENCE_ROOT")
+    return Path(env) if env else ROOT.parent / "reference"
+
+
+def stage_weights(ref_root: str | os.PathLike | None = None) -> Path:
     """Copies the reference's embedded ProteinMPNN v_48_020 weight image into
     ``hikoboshi_b200/weights/`` (SHA-256 checked) when it is not there yet."""
     import hashlib
@@ -100,7 +107,7 @@ def stage_weights(reference_root: str = "/root/reference") -> Path:
     dst = PKG / "weights" / WEIGHTS_NAME
     if dst.exists():
         return dst
-    src = Path(reference_root) / "weights" / WEIGHTS_NAME
+    src = Path(ref_root if ref_root is not None else reference_root()) / "weights" / WEIGHTS_NAME
     if not src.exists():
         raise FileNotFoundError(
             f"{dst} is missing and no reference checkout provides {WEIGHTS_NAME}")

@@ -793,21 +793,12 @@ __global__ void __launch_bounds__(kEncThreads, 1) dec_tables_tc_kernel(DecTables
   if (warp == 0) tmem_dealloc(tm, 512);
 }
 
-template <typename K>
-void set_smem(K kernel, uint32_t bytes) {
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-}
-
 }  // namespace
 
 void launch_enc_node_tc(cudaStream_t st, const EncNodeTcArgs& p, int num_sms) {
   const int tiles = (p.bv.total_residues + kNodeRes - 1) / kNodeRes;
   if (tiles <= 0) return;
-  static bool attr = false;
-  if (!attr) {
-    set_smem(enc_node_tc_kernel, kNodeSmem);
-    attr = true;
-  }
+  ensure_dynamic_smem((const void*)enc_node_tc_kernel, (int)kNodeSmem);
   const int grid = tiles < num_sms ? tiles : num_sms;
   enc_node_tc_kernel<<<grid, kEncThreads, kNodeSmem, st>>>(p);
 }
@@ -815,11 +806,7 @@ void launch_enc_node_tc(cudaStream_t st, const EncNodeTcArgs& p, int num_sms) {
 void launch_enc_featurize_tc(cudaStream_t st, const EncFeatTcArgs& p, int num_sms) {
   const int64_t tiles = ((int64_t)p.bv.total_residues * kK + 127) / 128;
   if (tiles <= 0) return;
-  static bool attr = false;
-  if (!attr) {
-    set_smem(enc_featurize_tc_kernel, kFeatSmem);
-    attr = true;
-  }
+  ensure_dynamic_smem((const void*)enc_featurize_tc_kernel, (int)kFeatSmem);
   const int grid = (int)(tiles < num_sms ? tiles : num_sms);
   enc_featurize_tc_kernel<<<grid, kEncThreads, kFeatSmem, st>>>(p);
 }
@@ -827,11 +814,7 @@ void launch_enc_featurize_tc(cudaStream_t st, const EncFeatTcArgs& p, int num_sm
 void launch_dec_tables_tc(cudaStream_t st, const DecTablesTcArgs& p, int num_sms) {
   const int64_t tiles = (p.rows + 127) / 128;
   if (tiles <= 0) return;
-  static bool attr = false;
-  if (!attr) {
-    set_smem(dec_tables_tc_kernel, kTabSmem);
-    attr = true;
-  }
+  ensure_dynamic_smem((const void*)dec_tables_tc_kernel, (int)kTabSmem);
   const int grid = (int)(tiles < num_sms ? tiles : num_sms);
   dec_tables_tc_kernel<<<grid, kEncThreads, kTabSmem, st>>>(p);
 }
@@ -839,11 +822,7 @@ void launch_dec_tables_tc(cudaStream_t st, const DecTablesTcArgs& p, int num_sms
 void launch_enc_edge_tc(cudaStream_t st, const EncEdgeTcArgs& p, int num_sms) {
   const int64_t tiles = ((int64_t)p.bv.total_residues * kK + 127) / 128;
   if (tiles <= 0) return;
-  static bool attr = false;
-  if (!attr) {
-    set_smem(enc_edge_tc_kernel, kEdgeSmem);
-    attr = true;
-  }
+  ensure_dynamic_smem((const void*)enc_edge_tc_kernel, (int)kEdgeSmem);
   const int grid = (int)(tiles < num_sms ? tiles : num_sms);
   enc_edge_tc_kernel<<<grid, kEncThreads, kEdgeSmem, st>>>(p);
 }

@@ -12,6 +12,8 @@
 #include <numeric>
 #include <thread>
 
+#include <sched.h>
+
 #include "host_order.hpp"
 #include "safetensors.hpp"
 
@@ -524,6 +526,15 @@ hkb_status validate_orders(const int32_t* modes, const int32_t* input_orders,
   return kOk;
 }
 
+// Cores this process may run on (its affinity mask), not the machine's: one
+// process per GPU on a shared host each gets its own slice.
+int usable_cores() {
+  cpu_set_t set;
+  CPU_ZERO(&set);
+  if (sched_getaffinity(0, sizeof(set), &set) == 0) return std::max(1, CPU_COUNT(&set));
+  return (int)std::max(1u, std::thread::hardware_concurrency());
+}
+
 // Per-sequence decoding orders of a validated batch (host threads).
 void generate_orders(const int32_t* modes, const int32_t* input_orders, HostBatch* hb) {
   hb->orders.assign(hb->Q, 0);
@@ -544,8 +555,7 @@ void generate_orders(const int32_t* modes, const int32_t* input_orders, HostBatc
     }
   };
   const int64_t work_items = hb->Q;
-  int nthreads = (int)std::min<int64_t>(std::max(1u, std::thread::hardware_concurrency()),
-                                        std::max<int64_t>(1, work_items / 16384));
+  int nthreads = (int)std::min<int64_t>(usable_cores(), std::max<int64_t>(1, work_items / 16384));
   nthreads = std::min(nthreads, 32);
   if (nthreads <= 1 || NS < 2) {
     work(0, NS);
@@ -843,10 +853,7 @@ hkb_status decode_f32(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
     return {HKB_UNAVAILABLE, "device allocation failed"};
   HKB_CUDA(cudaMemcpyAsync(d_g0, g0.data(), sizeof(int) * ng, cudaMemcpyHostToDevice, st));
   HKB_CUDA(cudaMemcpyAsync(d_gc, gc.data(), sizeof(int) * ng, cudaMemcpyHostToDevice, st));
-  HKB_CUDA(cudaMemcpyAsync(seeds, hb.seq_seed.data(), sizeof(uint64_t) * hb.NS,
-                           cudaMemcpyHostToDevice, st));
-  HKB_CUDA(cudaMemcpyAsync(temps, hb.seq_temp.data(), sizeof(float) * hb.NS,
-                           cudaMemcpyHostToDevice, st));
+  // seeds and temperatures were uploaded with the decoding orders
   HKB_CUDA(cudaMemsetAsync(PV, 0, sizeof(float) * 2 * hb.Q * kH, st));
   ArArgs a{};
   a.group_seq0 = d_g0;
@@ -941,10 +948,7 @@ hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   HKB_CUDA(cudaMemcpyAsync(d_g0, gseq.data(), sizeof(int) * gseq.size(), cudaMemcpyHostToDevice,
                            st));
   HKB_CUDA(cudaMemcpyAsync(d_gc, gc.data(), sizeof(int) * ng, cudaMemcpyHostToDevice, st));
-  HKB_CUDA(cudaMemcpyAsync(seeds, hb.seq_seed.data(), sizeof(uint64_t) * hb.NS,
-                           cudaMemcpyHostToDevice, st));
-  HKB_CUDA(cudaMemcpyAsync(temps, hb.seq_temp.data(), sizeof(float) * hb.NS,
-                           cudaMemcpyHostToDevice, st));
+  // seeds and temperatures were uploaded with the decoding orders
   ArBf16Args a{};
   a.group_seqs = d_g0;
   a.group_count = d_gc;
@@ -977,6 +981,117 @@ hkb_status check_device_error(hkb_engine* e) {
 }
 
 
+// Pinned staging for host-recomputed orders, `rows` entries; waits for the
+// previous upload out of it first.
+hkb_status order_staging(hkb_engine* e, int64_t rows, int32_t** out) {
+  if (e->h_orders_cap < (size_t)rows) {
+    if (e->h_orders) {
+      HKB_CUDA(cudaEventSynchronize(e->ev_orders));
+      cudaFreeHost(e->h_orders);
+      e->h_orders = nullptr;
+      e->h_orders_cap = 0;
+    }
+    if (cudaMallocHost(&e->h_orders, sizeof(int32_t) * rows) != cudaSuccess) {
+      cudaGetLastError();
+      e->h_orders = nullptr;
+      return {HKB_UNAVAILABLE, "host allocation failed"};
+    }
+    e->h_orders_cap = rows;
+  } else {
+    HKB_CUDA(cudaEventSynchronize(e->ev_orders));
+  }
+  *out = e->h_orders;
+  return kOk;
+}
+
+// Queues the device decoding-order kernel into `orders` [Q] and the read-back
+// of the list of sequences the host must recompute.
+hkb_status launch_orders(hkb_engine* e, const HostBatch& hb, const hkb_design_batch* batch,
+                         const DeviceBatch& db, int32_t* orders) {
+  auto& ws = e->ws;
+  cudaStream_t st = e->stream;
+  uint64_t* seeds = ws.get_as<uint64_t>("a.seed", hb.NS);
+  float* temps = ws.get_as<float>("a.temp", hb.NS);
+  int* modes = ws.get_as<int>("o.modes", hb.B);
+  unsigned int* rc = ws.get_as<unsigned int>("o.recheck", 1 + kRecheckCap);
+  if (!seeds || !temps || !modes || !rc) return {HKB_UNAVAILABLE, "device allocation failed"};
+  HKB_CUDA(cudaMemcpyAsync(seeds, hb.seq_seed.data(), sizeof(uint64_t) * hb.NS,
+                           cudaMemcpyHostToDevice, st));
+  HKB_CUDA(cudaMemcpyAsync(temps, hb.seq_temp.data(), sizeof(float) * hb.NS,
+                           cudaMemcpyHostToDevice, st));
+  std::vector<int> m(hb.B);
+  bool any_input = false;
+  for (int b = 0; b < hb.B; ++b) {
+    m[b] = batch->decode_orders ? batch->decode_orders[b] : HKB_DECODE_RANDOM;
+    any_input |= m[b] == HKB_DECODE_INPUT;
+  }
+  HKB_CUDA(cudaMemcpyAsync(modes, m.data(), sizeof(int) * hb.B, cudaMemcpyHostToDevice, st));
+  OrderArgs oa;
+  oa.bv = db.bv;
+  oa.sources = db.sources;
+  oa.modes = modes;
+  if (any_input) {
+    int32_t* io = ws.get_as<int32_t>("o.input", hb.R);
+    if (!io) return {HKB_UNAVAILABLE, "device allocation failed"};
+    HKB_CUDA(cudaMemcpyAsync(io, batch->input_orders, sizeof(int32_t) * hb.R,
+                             cudaMemcpyHostToDevice, st));
+    HKB_CUDA(cudaStreamSynchronize(st));   // pageable source: copy before returning
+    oa.input_orders = io;
+  }
+  oa.seeds = seeds;
+  oa.orders = orders;
+  oa.recheck_count = rc;
+  oa.recheck_list = reinterpret_cast<int*>(rc + 1);
+  oa.recheck_cap = kRecheckCap;
+  oa.recheck_all = e->recheck_all_orders;
+  oa.err = e->d_err;
+  HKB_CUDA(cudaMemsetAsync(rc, 0, sizeof(unsigned int), st));
+  launch_decode_orders(st, oa);
+  e->launches += 1;
+  HKB_CUDA(cudaMemcpyAsync(e->h_recheck, rc, sizeof(unsigned int) * (1 + kRecheckCap),
+                           cudaMemcpyDeviceToHost, st));
+  HKB_CUDA(cudaEventRecord(e->ev_recheck, st));
+  return kOk;
+}
+
+// Waits for the order kernel's recheck list and recomputes the listed
+// sequences' random orders with the host libm (the reference's arithmetic),
+// uploading them over the device's before the decode reads them.
+hkb_status finish_orders(hkb_engine* e, HostBatch& hb, const hkb_design_batch* batch,
+                         int32_t* orders) {
+  HKB_CUDA(cudaEventSynchronize(e->ev_recheck));
+  const unsigned int n = e->h_recheck[0];
+  if (n == 0) return kOk;
+  std::vector<int> list;
+  if (n <= (unsigned int)kRecheckCap) {
+    list.assign(reinterpret_cast<const int*>(e->h_recheck + 1),
+                reinterpret_cast<const int*>(e->h_recheck + 1) + n);
+    std::sort(list.begin(), list.end());
+  } else {
+    for (int sq = 0; sq < hb.NS; ++sq) {
+      const int mode = batch->decode_orders ? batch->decode_orders[hb.seq_prot[sq]]
+                                            : HKB_DECODE_RANDOM;
+      if (mode == HKB_DECODE_RANDOM) list.push_back(sq);
+    }
+  }
+  int64_t rows = 0;
+  for (int sq : list) rows += hb.L[hb.seq_prot[sq]];
+  int32_t* stage = nullptr;
+  hkb_status s = order_staging(e, rows, &stage);
+  if (s.code != HKB_OK) return s;
+  int64_t at = 0;
+  for (int sq : list) {
+    const int b = hb.seq_prot[sq];
+    random_decode_order(hb.mask.data() + hb.off[b], hb.L[b], hb.seq_seed[sq], stage + at);
+    HKB_CUDA(cudaMemcpyAsync(orders + hb.seq_row_off[sq], stage + at, sizeof(int32_t) * hb.L[b],
+                             cudaMemcpyHostToDevice, e->stream));
+    at += hb.L[b];
+  }
+  HKB_CUDA(cudaEventRecord(e->ev_orders, e->stream));
+  e->orders_rechecked += (int64_t)list.size();
+  return kOk;
+}
+
 hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
                          const uint8_t* host_src, const float* d_coords,
                          const uint8_t* d_src, HostBatch* hb,
@@ -1008,6 +1123,11 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
   s = upload_tables(e, *hb, &db);
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[0], st));
+  // Decoding orders on the device, ahead of the encoder; the host only
+  // recomputes the rare sequences the kernel marks (after the encoder is
+  // queued, so the wait overlaps device work).
+  s = launch_orders(e, *hb, batch, db, out.orders);
+  if (s.code != HKB_OK) return s;
   EncoderOut eo;
   // fp32: SIMT parity pipeline; bf16: fp32 encoder, tables rounded to bf16;
   // f16: tensor-core encoder writing fp16 tables.
@@ -1025,29 +1145,8 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
       s = decoder_tables_bf16(e, *hb, eo, dt, &tb);
   }
   if (s.code != HKB_OK) return s;
-  // The decoding orders are only needed by the decode loop: generate them on
-  // the host while the encoder and tables run on the device.
-  generate_orders(batch->decode_orders, batch->input_orders, hb);
-  if (e->h_orders_cap < (size_t)hb->Q) {
-    if (e->h_orders) {
-      HKB_CUDA(cudaEventSynchronize(e->ev_orders));
-      cudaFreeHost(e->h_orders);
-      e->h_orders = nullptr;
-      e->h_orders_cap = 0;
-    }
-    if (cudaMallocHost(&e->h_orders, sizeof(int32_t) * hb->Q) != cudaSuccess) {
-      cudaGetLastError();
-      e->h_orders = nullptr;
-      return {HKB_UNAVAILABLE, "host allocation failed"};
-    }
-    e->h_orders_cap = hb->Q;
-  } else {
-    HKB_CUDA(cudaEventSynchronize(e->ev_orders));   // previous upload done
-  }
-  std::memcpy(e->h_orders, hb->orders.data(), sizeof(int32_t) * hb->Q);
-  HKB_CUDA(cudaMemcpyAsync(out.orders, e->h_orders, sizeof(int32_t) * hb->Q,
-                           cudaMemcpyHostToDevice, st));
-  HKB_CUDA(cudaEventRecord(e->ev_orders, st));
+  s = finish_orders(e, *hb, batch, out.orders);
+  if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[2], st));
   s = e->precision == HKB_PRECISION_FP32 ? decode_f32(e, *hb, db, eo, dt, out)
                                           : decode_tc(e, *hb, db, eo, tb, out);
@@ -1110,7 +1209,17 @@ hkb_status hkb_mpnn_create(const void* st_blob, size_t length, int device,
   e->weights_bytes = P.blob.data.size() * sizeof(float);
   for (auto& ev : e->ev) cudaEventCreate(&ev);
   cudaEventCreateWithFlags(&e->ev_orders, cudaEventDisableTiming);
+  cudaEventCreateWithFlags(&e->ev_recheck, cudaEventDisableTiming);
   cudaEventRecord(e->ev_orders, e->stream);
+  if (cudaMallocHost(&e->h_recheck, sizeof(unsigned int) * (1 + kRecheckCap)) != cudaSuccess) {
+    cudaGetLastError();
+    e->h_recheck = nullptr;
+    hkb_mpnn_destroy(e);
+    return {HKB_UNAVAILABLE, "host allocation failed"};
+  }
+  // Test hook: HKB_RECHECK_ALL_ORDERS=1 sends every random order through the
+  // host recomputation path.
+  if (const char* v = std::getenv("HKB_RECHECK_ALL_ORDERS")) e->recheck_all_orders = v[0] == '1';
   if (cudaMemcpy(e->d_weights, P.blob.data.data(), e->weights_bytes,
                  cudaMemcpyHostToDevice) != cudaSuccess) {
     cudaGetLastError();
@@ -1183,6 +1292,8 @@ void hkb_mpnn_destroy(hkb_engine* e) {
   for (auto& ev : e->ev)
     if (ev) cudaEventDestroy(ev);
   if (e->ev_orders) cudaEventDestroy(e->ev_orders);
+  if (e->ev_recheck) cudaEventDestroy(e->ev_recheck);
+  if (e->h_recheck) cudaFreeHost(e->h_recheck);
   if (e->h_orders) cudaFreeHost(e->h_orders);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
@@ -1237,9 +1348,11 @@ hkb_status hkb_mpnn_design(hkb_engine* e, const hkb_design_batch* batch,
   if (out->scores)
     HKB_CUDA(cudaMemcpyAsync(out->scores, o.scores, sizeof(float) * NS,
                              cudaMemcpyDeviceToHost, st));
+  if (out->orders)
+    HKB_CUDA(cudaMemcpyAsync(out->orders, o.orders, sizeof(int32_t) * Q,
+                             cudaMemcpyDeviceToHost, st));
   s = check_device_error(e);
   if (s.code != HKB_OK) return s;
-  if (out->orders) std::memcpy(out->orders, hb.orders.data(), sizeof(int32_t) * Q);
   record_timings(e);
   return kOk;
 }

@@ -13,6 +13,9 @@
 
 namespace hkb {
 
+// Capacity of the device decoding-order kernel's recheck list.
+constexpr int kRecheckCap = 255;
+
 // Named, grow-only device buffers reused across calls.
 class Workspace {
  public:
@@ -91,4 +94,11 @@ struct hkb_engine {
   int32_t* h_orders = nullptr;
   size_t h_orders_cap = 0;
   cudaEvent_t ev_orders = nullptr;
+  // device decoding orders: pinned read-back of the recheck count and list
+  // ([0] count, then up to kRecheckCap sequence indices), its event, and the
+  // number of sequences the host has recomputed so far
+  unsigned int* h_recheck = nullptr;
+  cudaEvent_t ev_recheck = nullptr;
+  int recheck_all_orders = 0;
+  int64_t orders_rechecked = 0;
 };

@@ -27,13 +27,8 @@ double uniform01(std::uint64_t& state) {
   return static_cast<double>(splitmix64_next(state) >> 11) * (1.0 / 9007199254740992.0);
 }
 
-void random_decode_order(const float* mask, int L, std::uint64_t seed,
-                         std::int32_t* order) {
-  struct Key {
-    float score;
-    std::int32_t index;
-  };
-  std::vector<Key> keys(static_cast<std::size_t>(L));
+void random_decode_order_into(const float* mask, int L, std::uint64_t seed, OrderKey* keys,
+                              std::int32_t* order) {
   std::uint64_t s = seed;
   for (int r = 0; r < L; ++r) {
     double u1 = uniform01(s);
@@ -45,11 +40,17 @@ void random_decode_order(const float* mask, int L, std::uint64_t seed,
     const float m = mask != nullptr ? mask[r] : 1.0F;
     keys[r] = {(m + 0.0001F) * z, r};
   }
-  std::sort(keys.begin(), keys.end(), [](const Key& a, const Key& b) {
+  std::sort(keys, keys + L, [](const OrderKey& a, const OrderKey& b) {
     if (a.score != b.score) return a.score < b.score;
     return a.index < b.index;
   });
   for (int p = 0; p < L; ++p) order[p] = keys[p].index;
+}
+
+void random_decode_order(const float* mask, int L, std::uint64_t seed,
+                         std::int32_t* order) {
+  std::vector<OrderKey> keys(static_cast<std::size_t>(L));
+  random_decode_order_into(mask, L, seed, keys.data(), order);
 }
 
 bool check_permutation(const std::int32_t* order, int L) {

@@ -6,6 +6,12 @@
 
 namespace hkb {
 
+// Raises `func`'s dynamic shared-memory limit to `bytes` on the current device,
+// once per (device, kernel, size).  The attribute is per device, and engines on
+// several devices or host threads launch the same kernels; the bookkeeping is
+// guarded by a mutex.
+void ensure_dynamic_smem(const void* func, int bytes);
+
 // Per-call device tables describing a batch.
 struct BatchView {
   int num_proteins = 0;
@@ -279,6 +285,25 @@ void convert_f32_to_16(cudaStream_t st, const float* src, uint16_t* dst, int64_t
 void launch_ar_decode_tc(cudaStream_t st, const BatchView& bv,
                          const Bf16DecodeWeights& w, const Bf16DecodeTables& t,
                          const ArBf16Args& a, bool f16, unsigned int* err);
+
+// Per-sequence decoding orders on the device (decode_order_scalar.cpp:61-116);
+// modes[b]: 0 random, 1 identity, 2 input_orders[off_b ..].  Sequences whose
+// random order the host must recompute (a score near a float rounding
+// midpoint, or recheck_all) are appended to recheck_list.
+struct OrderArgs {
+  BatchView bv;
+  const uint8_t* sources = nullptr;     // [R,5] atom sources (mask = N, CA, C, O present)
+  const int* modes = nullptr;           // [B]
+  const int32_t* input_orders = nullptr;  // [R] (mode 2 only)
+  const uint64_t* seeds = nullptr;      // [NS]
+  int32_t* orders = nullptr;            // [Q] out
+  unsigned int* recheck_count = nullptr;
+  int* recheck_list = nullptr;
+  int recheck_cap = 0;
+  int recheck_all = 0;
+  unsigned int* err = nullptr;
+};
+void launch_decode_orders(cudaStream_t st, const OrderArgs& a);
 
 void launch_scores(cudaStream_t st, const BatchView& bv, const int* tokens,
                    const float* log_probs, const float* mask, float* scores);

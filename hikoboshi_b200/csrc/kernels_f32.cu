@@ -13,8 +13,33 @@
 #include "kernels.hpp"
 
 #include <algorithm>
+#include <mutex>
 
 namespace hkb {
+
+void ensure_dynamic_smem(const void* func, int bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  // A fixed table (no heap allocation: the allocation-free entry point runs
+  // through here too).  Past its capacity the attribute is simply set again.
+  struct Entry {
+    int dev;
+    const void* func;
+    int bytes;
+  };
+  constexpr int kCap = 512;
+  static Entry done[kCap];
+  static int n_done = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n_done; ++i)
+    if (done[i].dev == dev && done[i].func == func && done[i].bytes == bytes) return;
+  cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (n_done < kCap) done[n_done++] = {dev, func, bytes};
+}
 
 namespace {
 
@@ -941,18 +966,10 @@ void gemm_f32x2(cudaStream_t st, int64_t M, int N, int K, const float* A, int ld
                 const float* B, int ldb, const float* bias, int act, void* C, int ldc,
                 bool out_f16) {
   if (M <= 0) return;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(gemm_f32x2_kernel<0, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kG2Smem);
-    cudaFuncSetAttribute(gemm_f32x2_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kG2Smem);
-    cudaFuncSetAttribute(gemm_f32x2_kernel<0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kG2Smem);
-    cudaFuncSetAttribute(gemm_f32x2_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kG2Smem);
-    attr_set = true;
-  }
+  ensure_dynamic_smem((const void*)gemm_f32x2_kernel<0, false>, (int)kG2Smem);
+  ensure_dynamic_smem((const void*)gemm_f32x2_kernel<1, false>, (int)kG2Smem);
+  ensure_dynamic_smem((const void*)gemm_f32x2_kernel<0, true>, (int)kG2Smem);
+  ensure_dynamic_smem((const void*)gemm_f32x2_kernel<1, true>, (int)kG2Smem);
   const dim3 grid((unsigned)((M + kG2Tile - 1) / kG2Tile), N / kG2Tile);
   if (out_f16) {
     if (act == 1)
@@ -973,12 +990,7 @@ void launch_knn(cudaStream_t st, const BatchView& bv, const float* coords,
   if (bv.total_residues <= 0) return;
   // One shared-memory key per candidate of the query's protein.
   const size_t smem = (size_t)max_len * sizeof(unsigned long long);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(knn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kMaxResidues * (int)sizeof(unsigned long long));
-    attr_set = true;
-  }
+  ensure_dynamic_smem((const void*)knn_kernel, kMaxResidues * (int)sizeof(unsigned long long));
   knn_kernel<<<bv.total_residues, 256, smem, st>>>(bv, coords, sources, e_idx, d2,
                                                    mask, err);
 }
@@ -1075,12 +1087,7 @@ void launch_ar_decode_f32(cudaStream_t st, const BatchView& bv, const F32Weights
                           const DecoderTables& dt, const ArArgs& a, unsigned int* err) {
   if (a.num_groups <= 0) return;
   const size_t smem = sizeof(ArSmem);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(ar_decode_f32_kernel,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_set = true;
-  }
+  ensure_dynamic_smem((const void*)ar_decode_f32_kernel, (int)smem);
   ar_decode_f32_kernel<<<a.num_groups, kArThreads, smem, st>>>(bv, w, dt, a, err);
 }
 

@@ -860,14 +860,8 @@ void launch_ar_decode_tc(cudaStream_t st, const BatchView& bv, const Bf16DecodeW
                          const Bf16DecodeTables& t, const ArBf16Args& a, bool f16,
                          unsigned int* err) {
   if (a.num_groups <= 0) return;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(ar_decode_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kSmemBytes);
-    cudaFuncSetAttribute(ar_decode_tc_kernel<false>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-    attr_set = true;
-  }
+  ensure_dynamic_smem((const void*)ar_decode_tc_kernel<true>, (int)kSmemBytes);
+  ensure_dynamic_smem((const void*)ar_decode_tc_kernel<false>, (int)kSmemBytes);
   if (f16)
     ar_decode_tc_kernel<true><<<a.num_groups, kThreadsB, kSmemBytes, st>>>(bv, w, t, a, err);
   else

@@ -118,30 +118,6 @@ T* at(unsigned char* base, Buf b) {
   return reinterpret_cast<T*>(base + offset_of(b));
 }
 
-// Random decoding order with stack storage only (same rule as
-// random_decode_order: ascending (mask + 1e-4) |z|, ties by index).
-void stack_random_order(const float* mask, int L, uint64_t seed, int32_t* order) {
-  struct Key {
-    float score;
-    int32_t index;
-  } keys[kMaxR];
-  uint64_t s = seed;
-  for (int r = 0; r < L; ++r) {
-    double u1 = uniform01(s);
-    if (u1 <= 0.0) u1 = 1.0 / 9007199254740992.0;
-    const double u2 = uniform01(s);
-    const double radius = std::sqrt(-2.0 * std::log(u1));
-    const float z = static_cast<float>(
-        std::fabs(radius * std::cos(6.283185307179586476925286766559 * u2)));
-    keys[r] = {(mask[r] + 0.0001F) * z, r};
-  }
-  std::sort(keys, keys + L, [](const Key& a, const Key& b) {
-    if (a.score != b.score) return a.score < b.score;
-    return a.index < b.index;
-  });
-  for (int p = 0; p < L; ++p) order[p] = keys[p].index;
-}
-
 #define NOALLOC_CUDA(call)                                                     \
   do {                                                                         \
     const cudaError_t ce_ = (call);                                            \
@@ -196,6 +172,7 @@ extern "C" hkb_status hkb_mpnn_design_noalloc(hkb_engine* e, const hkb_design_ba
   uint64_t seeds[kMaxNS];
   float temps[kMaxNS], mask[kMaxR];
   int32_t orders[kMaxQ];
+  OrderKey keys[kMaxR];
   NOALLOC_CUDA(cudaMemcpyAsync(hsrc, batch->atom_sources, (size_t)R * 5, cudaMemcpyDeviceToHost, st));
   NOALLOC_CUDA(cudaStreamSynchronize(st));
   int r0 = 0, s0 = 0, max_len = 0, ng = 0;
@@ -232,7 +209,7 @@ extern "C" hkb_status hkb_mpnn_design_noalloc(hkb_engine* e, const hkb_design_ba
       seeds[sq] = (batch->seeds ? batch->seeds[b] : 0ull) + (uint64_t)q;
       temps[sq] = batch->temperatures ? batch->temperatures[b] : 0.1f;
       int32_t* o = orders + seq_row[sq];
-      if (mode == HKB_DECODE_RANDOM) stack_random_order(mask + r0, L, seeds[sq], o);
+      if (mode == HKB_DECODE_RANDOM) random_decode_order_into(mask + r0, L, seeds[sq], keys, o);
       else if (mode == HKB_DECODE_N_TO_C) for (int p = 0; p < L; ++p) o[p] = p;
       else std::memcpy(o, batch->input_orders + r0, sizeof(int32_t) * L);
     }

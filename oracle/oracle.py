@@ -93,6 +93,10 @@ def _p(a):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
+class _Status(ctypes.Structure):
+    _fields_ = [("code", ctypes.c_int32), ("detail", ctypes.c_char_p)]
+
+
 class Oracle:
     """The C restatement, bound to one weight file."""
 
@@ -218,6 +222,18 @@ class RefLib:
         st = self.lib.ref_load_weights(str(weights_path).encode())
         if st != 0:
             raise RuntimeError(f"ref_load_weights failed ({st})")
+
+    def synthetic_backbone(self, seed: int, residue_count: int):
+        """The benchmark's seeded backbone generator (the engine's own
+        host_synth.cpp, linked into this library) without loading the engine."""
+        c = np.zeros((residue_count, 5, 3), np.float32)
+        s = np.zeros((residue_count, 5), np.uint8)
+        fn = self.lib.ref_synthetic_backbone
+        fn.restype = _Status
+        st = fn(ctypes.c_uint64(seed), ctypes.c_int32(residue_count), _p(c), _p(s))
+        if st.code != 0:
+            raise ValueError((st.detail or b"").decode())
+        return c, s
 
     def knn(self, coords, sources):
         coords, sources = _f32(coords), _u8(sources)

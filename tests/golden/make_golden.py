@@ -1,9 +1,10 @@
 #!/usr/bin/env python3
 """Regenerate the committed golden fixtures under tests/golden/.
 
-Run in the build container, where the reference checkout is mounted:
+Run where the reference checkout is available ($HKB_REFERENCE_ROOT, or a
+checkout named ``reference`` beside this repository):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref <reference checkout>]
 
 1. ``upstream_fixtures.json`` -- the reference's five ProteinMPNN v_48_020
    parity fixtures (tests/parity/proteinmpnn_v48_020/fixtures/*.{pdb,
@@ -163,8 +164,11 @@ def synthetic(ref):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=None)
     args = ap.parse_args()
+    if args.ref is None:
+        from hikoboshi_b200._build import reference_root
+        args.ref = str(reference_root())
     from oracle.oracle import RefLib, build
 
     build(ref=True)

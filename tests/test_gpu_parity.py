@@ -157,3 +157,63 @@ def test_design_validation_matches_reference(engine_fp32):
         engine_fp32.design([np.zeros((0, 5, 3), np.float32)], [np.zeros((0, 5), np.uint8)],
                            num_seqs=1)
     assert e.value.code == 1 and "at least one residue" in e.value.detail
+
+
+def test_config1_design_matches_reference(engine_fp32):
+    """BASELINE config 1 as the reference runs it: one synthetic backbone of
+    L=128 (seed 7), 8 sequences, T=0.1, random decoding order, seed 7.  The
+    reference's own design path (compiled from its sources) and the fp32
+    engine give the same orders and tokens, and log-probs within 1e-4 / T."""
+    from hikoboshi_b200 import synthetic_backbone
+    from oracle.oracle import RefLib
+    from conftest import WEIGHTS
+    c, s = synthetic_backbone(7, 128)
+    ref = RefLib(WEIGHTS)
+    tok_r, lp_r, sc_r = ref.design(c, s, 8, seed=7, temperature=0.1, decode_order=0)
+    res = engine_fp32.design([c], [s], num_seqs=8, seeds=7, temperatures=0.1)
+    from hikoboshi_b200 import decode_order
+    for q in range(8):
+        assert (res.orders[0][q] == decode_order(128, 7 + q)).all(), q
+    assert (res.tokens[0] == tok_r).all()
+    assert np.abs(res.log_probs[0] - lp_r).max() <= tf_tol(0.1)
+    assert np.abs(res.scores[0] - sc_r).max() <= tf_tol(0.1)
+
+
+def test_device_orders_match_host_orders(weights_path):
+    """Random decoding orders are generated on the device; the host libm path
+    (the reference's arithmetic) must give the same permutation for every
+    sequence, with masked residues and lengths from 1 to 1024.  A second
+    engine sends every sequence through the host recomputation path, and both
+    engines must then produce identical designs."""
+    import os
+    from hikoboshi_b200 import DesignEngine, decode_order, synthetic_backbone
+    Ls = [1, 2, 31, 48, 256, 257, 1024]
+    bb = [synthetic_backbone(300 + i, L) for i, L in enumerate(Ls)]
+    coords = [x[0] for x in bb]
+    sources = [x[1].copy() for x in bb]
+    sources[4][[3, 100, 200], 0] = 0   # masked residues: score factor 1e-4
+    S = [5, 3, 64, 64, 200, 64, 40]
+    seeds = [0, 2 ** 63 + 5, 17, 99, 123456789, 7, 2 ** 64 - 3]
+    eng = DesignEngine(weights_path, device=0, precision="f16")
+    try:
+        res = eng.design(coords, sources, num_seqs=S, seeds=seeds, temperatures=0.1)
+    finally:
+        eng.close()
+    for b, L in enumerate(Ls):
+        mask = (sources[b][:, :4].min(axis=1) > 0).astype(np.float32)
+        for q in range(S[b]):
+            want = decode_order(L, (seeds[b] + q) % 2 ** 64, mask=mask)
+            assert (res.orders[b][q] == want).all(), (b, q)
+    os.environ["HKB_RECHECK_ALL_ORDERS"] = "1"
+    try:
+        eng2 = DesignEngine(weights_path, device=0, precision="f16")
+    finally:
+        del os.environ["HKB_RECHECK_ALL_ORDERS"]
+    try:
+        res2 = eng2.design(coords, sources, num_seqs=S, seeds=seeds, temperatures=0.1)
+    finally:
+        eng2.close()
+    for b in range(len(Ls)):
+        assert (res2.orders[b] == res.orders[b]).all()
+        assert (res2.tokens[b] == res.tokens[b]).all()
+        assert (res2.log_probs[b] == res.log_probs[b]).all()

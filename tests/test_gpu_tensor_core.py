@@ -66,7 +66,7 @@ def test_tensor_core_design_matches_oracle(request, oracle, precision, tol):
         assert (again.log_probs[b] == res.log_probs[b]).all()
 
 
-def test_f16_full_size_properties(engine_f16, oracle):
+def test_f16_full_size_properties(engine_f16, engine_fp32, oracle):
     """Config-2 sized batch (64 x L=256 x 32): properties that hold at any
     size -- valid tokens, each emitted row a normalised distribution,
     scores equal to the mean NLL of the emitted rows, orders are the
@@ -86,10 +86,35 @@ def test_f16_full_size_properties(engine_f16, oracle):
         for s in (0, 31):
             assert (res.orders[b][s] == decode_order(256, b + s)).all()
     # (1, 0) and (1, 9) share a decode CTA with sequences of protein 0 (the
-    # 2048 sequences of equal length are packed into 148 groups of 13-14)
+    # 2048 sequences of equal length are packed into 147 groups of 13-14)
     for b, s in ((0, 0), (1, 0), (1, 9), (40, 31)):
         check_design(oracle, coords[b], sources[b], res.tokens[b][s], res.log_probs[b][s],
                      res.orders[b][s], b + s, 0.1, 2e-2 / 0.1)
+    # one sequence of every decode CTA (its first and, for the last group, its
+    # last) against the fp32 engine's teacher-forced pass on the same tokens
+    # and orders (the fp32 engine is pinned to the reference)
+    G = -(-2048 // 148)
+    ng = -(-2048 // G)
+    base, extra = divmod(2048, ng)
+    starts = np.cumsum([0] + [base + (1 if g < extra else 0) for g in range(ng)])
+    picks = sorted(set(int(x) for x in starts[:-1]) | {2047})
+    assert len(picks) >= 147
+    by_prot = {}
+    for q in picks:
+        by_prot.setdefault(q // 32, []).append(q % 32)
+    prots = sorted(by_prot)
+    tf = engine_fp32.score([coords[b] for b in prots], [sources[b] for b in prots],
+                           [res.tokens[b][by_prot[b]] for b in prots],
+                           orders=[res.orders[b][by_prot[b]] for b in prots])
+    from parity_util import check_against
+    checked = 0
+    for (lp32, _, _), b in zip(tf, prots):
+        mask = sources[b][:, :4].min(axis=1) > 0
+        for i, s in enumerate(by_prot[b]):
+            check_against(oracle.uniform, _scaled(lp32[i], 0.1), mask, res.tokens[b][s],
+                          res.log_probs[b][s], res.orders[b][s], b + s, 0.1, 2e-2 / 0.1)
+            checked += 1
+    assert checked == len(picks)
 
 
 def _scaled(lp_unscaled, T):

@@ -7,7 +7,10 @@ scratch is one fixed device array inside the library, so this test checks
 that two calls in a row -- the second reusing whatever the first left in
 that array -- both reproduce the allocating device entry point
 (hkb_mpnn_design_device) on the same fp32 engine, and that a batch over the
-limit is refused with InvalidArgument.
+limit is refused with InvalidArgument.  The two entry points run the same
+kernels on the same inputs, so their outputs must be bit-identical; the
+random, N-to-C and caller-given decoding orders are all exercised, and the
+device's free memory must not move across a call.
 
 This file is named so that pytest collects it last.
 """
@@ -21,12 +24,13 @@ pytestmark = pytest.mark.gpu
 P = ctypes.POINTER
 
 
-def _batch(hl, L, S, seeds, temps, modes, coords_ptr, src_ptr):
+def _batch(hl, L, S, seeds, temps, modes, coords_ptr, src_ptr, input_orders=None):
+    io = None if input_orders is None else input_orders.ctypes.data_as(P(ctypes.c_int32))
     return hl.DesignBatch(len(L), L.ctypes.data_as(P(ctypes.c_int32)), coords_ptr, src_ptr,
                           S.ctypes.data_as(P(ctypes.c_int32)),
                           seeds.ctypes.data_as(P(ctypes.c_uint64)),
                           temps.ctypes.data_as(P(ctypes.c_float)),
-                          modes.ctypes.data_as(P(ctypes.c_int32)), None)
+                          modes.ctypes.data_as(P(ctypes.c_int32)), io)
 
 
 def _outputs(torch, hl, Q, NS):
@@ -39,7 +43,8 @@ def _outputs(torch, hl, Q, NS):
     return out, (t, lp, o, sc)
 
 
-def test_noalloc_design_matches_device_design_twice(weights_path):
+@pytest.mark.parametrize("modes", [(0, 0), (1, 2)], ids=["random", "n_to_c+input"])
+def test_noalloc_design_matches_device_design_twice(weights_path, modes):
     import torch
     from hikoboshi_b200 import DesignEngine, synthetic_backbone
     from hikoboshi_b200 import _lib as hl
@@ -52,34 +57,44 @@ def test_noalloc_design_matches_device_design_twice(weights_path):
         S = np.array([3, 2], np.int32)
         seeds = np.array([11, 500], np.uint64)
         temps = np.array([0.1, 0.0], np.float32)
-        modes = np.array([0, 0], np.int32)
+        modes_a = np.array(modes, np.int32)
+        # a caller permutation for every protein (read where the mode is INPUT)
+        rng = np.random.default_rng(5)
+        io = np.concatenate([rng.permutation(n).astype(np.int32) for n in Ls])
         bb = [synthetic_backbone(40 + i, n) for i, n in enumerate(Ls)]
         coords = torch.from_numpy(np.concatenate([b[0] for b in bb])).cuda()
         srcs = torch.from_numpy(np.concatenate([b[1] for b in bb])).cuda()
         Q = int((L * S).sum())
         NS = int(S.sum())
-        batch = _batch(hl, L, S, seeds, temps, modes, ctypes.c_void_p(coords.data_ptr()),
-                       ctypes.c_void_p(srcs.data_ptr()))
+        batch = _batch(hl, L, S, seeds, temps, modes_a, ctypes.c_void_p(coords.data_ptr()),
+                       ctypes.c_void_p(srcs.data_ptr()), io)
 
         ref_out, ref = _outputs(torch, hl, Q, NS)
         hl.check(lib.hkb_mpnn_design_device(eng._h, ctypes.byref(batch), ctypes.byref(ref_out),
                                             None))
         torch.cuda.synchronize()
         ref = [x.cpu().numpy() for x in ref]
+        if modes[1] == 2:
+            assert (ref[2][3 * 24:].reshape(2, 40) == io[24:]).all()
+        if modes[0] == 1:
+            assert (ref[2][:3 * 24].reshape(3, 24) == np.arange(24)).all()
 
-        for call in range(2):
-            out, got = _outputs(torch, hl, Q, NS)
+        outs = [_outputs(torch, hl, Q, NS) for _ in range(2)]   # allocated up front
+        free = []
+        for call, (out, got) in enumerate(outs):
             hl.check(lib.hkb_mpnn_design_noalloc(eng._h, ctypes.byref(batch), ctypes.byref(out),
                                                  None))
             torch.cuda.synchronize()
+            free.append(torch.cuda.mem_get_info()[0])
             tok, lp, order, sc = [x.cpu().numpy() for x in got]
+            # same kernels on the same inputs: bit-identical outputs
             assert (order == ref[2]).all(), call
             assert (tok == ref[0]).all(), call
-            # same kernels and same inputs: within the fp32 parity tolerance
-            # on temperature-scaled log-probs (1e-4 / T, T = 0.1)
-            assert np.abs(lp - ref[1]).max() <= 1e-3, call
-            assert np.abs(sc - ref[3]).max() <= 1e-3, call
+            assert (lp.view(np.uint32) == ref[1].view(np.uint32)).all(), call
+            assert (sc.view(np.uint32) == ref[3].view(np.uint32)).all(), call
             assert np.isfinite(lp).all() and ((tok >= 0) & (tok < 21)).all()
+        # nothing was allocated on the device by the second call
+        assert free[0] == free[1]
     finally:
         eng.close()
 
