@@ -792,7 +792,7 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
 
 // Decoder tables straight to 16-bit (fp16 mode) for the fused decode kernel.
 hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const EncoderOut& eo,
-                             Bf16DecodeTables* tb) {
+                             Bf16DecodeTables* tb, bool with_pe = true) {
   auto& ws = e->ws;
   cudaStream_t st = e->stream;
   const int64_t R = hb.R, SL = R * kK;
@@ -801,9 +801,9 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const EncoderOu
   ta.rows = SL;
   ta.err = e->d_err;
   for (int l = 0; l < 3; ++l) {
-    uint16_t* pe = ws.get_as<uint16_t>("b.PE" + std::to_string(l), SL * kH);
+    uint16_t* pe = with_pe ? ws.get_as<uint16_t>("b.PE" + std::to_string(l), SL * kH) : nullptr;
     uint16_t* pv = ws.get_as<uint16_t>("b.PVenc" + std::to_string(l), R * kH);
-    if (!pe || !pv) return {HKB_UNAVAILABLE, "device allocation failed"};
+    if ((with_pe && !pe) || !pv) return {HKB_UNAVAILABLE, "device allocation failed"};
     const std::string q = "dec" + std::to_string(l) + ".";
     ta.W[l] = e->gemm_img.at(q + "W1b");
     ta.out[l] = pe;
@@ -812,7 +812,8 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const EncoderOu
     tb->PE[l] = pe;
     tb->PVenc[l] = pv;
   }
-  launch_dec_tables_tc(st, ta, e->num_sms);
+  // (the teacher-forced pass forms W1b h_E by MMA from h_E itself)
+  if (with_pe) launch_dec_tables_tc(st, ta, e->num_sms);
   float* a0 = ws.get_as<float>("d.Aenc0", R * kH);
   if (!a0) return {HKB_UNAVAILABLE, "device allocation failed"};
   gemm_f32(st, R, kH, kH, eo.h_v, kH, e->w32.dec[0].W1aT, kH, e->w32.dec[0].b1, 0, a0, kH);
@@ -1006,8 +1007,8 @@ hkb_status order_staging(hkb_engine* e, int64_t rows, int32_t** out) {
 
 // Queues the device decoding-order kernel into `orders` [Q] and the read-back
 // of the list of sequences the host must recompute.
-hkb_status launch_orders(hkb_engine* e, const HostBatch& hb, const hkb_design_batch* batch,
-                         const DeviceBatch& db, int32_t* orders) {
+hkb_status launch_orders(hkb_engine* e, const HostBatch& hb, const int32_t* modes_in,
+                         const int32_t* input_orders, const DeviceBatch& db, int32_t* orders) {
   auto& ws = e->ws;
   cudaStream_t st = e->stream;
   uint64_t* seeds = ws.get_as<uint64_t>("a.seed", hb.NS);
@@ -1017,12 +1018,13 @@ hkb_status launch_orders(hkb_engine* e, const HostBatch& hb, const hkb_design_ba
   if (!seeds || !temps || !modes || !rc) return {HKB_UNAVAILABLE, "device allocation failed"};
   HKB_CUDA(cudaMemcpyAsync(seeds, hb.seq_seed.data(), sizeof(uint64_t) * hb.NS,
                            cudaMemcpyHostToDevice, st));
-  HKB_CUDA(cudaMemcpyAsync(temps, hb.seq_temp.data(), sizeof(float) * hb.NS,
-                           cudaMemcpyHostToDevice, st));
+  if (hb.seq_temp.size() == (size_t)hb.NS)
+    HKB_CUDA(cudaMemcpyAsync(temps, hb.seq_temp.data(), sizeof(float) * hb.NS,
+                             cudaMemcpyHostToDevice, st));
   std::vector<int> m(hb.B);
   bool any_input = false;
   for (int b = 0; b < hb.B; ++b) {
-    m[b] = batch->decode_orders ? batch->decode_orders[b] : HKB_DECODE_RANDOM;
+    m[b] = modes_in ? modes_in[b] : HKB_DECODE_RANDOM;
     any_input |= m[b] == HKB_DECODE_INPUT;
   }
   HKB_CUDA(cudaMemcpyAsync(modes, m.data(), sizeof(int) * hb.B, cudaMemcpyHostToDevice, st));
@@ -1033,7 +1035,7 @@ hkb_status launch_orders(hkb_engine* e, const HostBatch& hb, const hkb_design_ba
   if (any_input) {
     int32_t* io = ws.get_as<int32_t>("o.input", hb.R);
     if (!io) return {HKB_UNAVAILABLE, "device allocation failed"};
-    HKB_CUDA(cudaMemcpyAsync(io, batch->input_orders, sizeof(int32_t) * hb.R,
+    HKB_CUDA(cudaMemcpyAsync(io, input_orders, sizeof(int32_t) * hb.R,
                              cudaMemcpyHostToDevice, st));
     HKB_CUDA(cudaStreamSynchronize(st));   // pageable source: copy before returning
     oa.input_orders = io;
@@ -1057,7 +1059,7 @@ hkb_status launch_orders(hkb_engine* e, const HostBatch& hb, const hkb_design_ba
 // Waits for the order kernel's recheck list and recomputes the listed
 // sequences' random orders with the host libm (the reference's arithmetic),
 // uploading them over the device's before the decode reads them.
-hkb_status finish_orders(hkb_engine* e, HostBatch& hb, const hkb_design_batch* batch,
+hkb_status finish_orders(hkb_engine* e, HostBatch& hb, const int32_t* modes_in,
                          int32_t* orders) {
   HKB_CUDA(cudaEventSynchronize(e->ev_recheck));
   const unsigned int n = e->h_recheck[0];
@@ -1069,8 +1071,7 @@ hkb_status finish_orders(hkb_engine* e, HostBatch& hb, const hkb_design_batch* b
     std::sort(list.begin(), list.end());
   } else {
     for (int sq = 0; sq < hb.NS; ++sq) {
-      const int mode = batch->decode_orders ? batch->decode_orders[hb.seq_prot[sq]]
-                                            : HKB_DECODE_RANDOM;
+      const int mode = modes_in ? modes_in[hb.seq_prot[sq]] : HKB_DECODE_RANDOM;
       if (mode == HKB_DECODE_RANDOM) list.push_back(sq);
     }
   }
@@ -1126,7 +1127,7 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
   // Decoding orders on the device, ahead of the encoder; the host only
   // recomputes the rare sequences the kernel marks (after the encoder is
   // queued, so the wait overlaps device work).
-  s = launch_orders(e, *hb, batch, db, out.orders);
+  s = launch_orders(e, *hb, batch->decode_orders, batch->input_orders, db, out.orders);
   if (s.code != HKB_OK) return s;
   EncoderOut eo;
   // fp32: SIMT parity pipeline; bf16: fp32 encoder, tables rounded to bf16;
@@ -1145,7 +1146,7 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
       s = decoder_tables_bf16(e, *hb, eo, dt, &tb);
   }
   if (s.code != HKB_OK) return s;
-  s = finish_orders(e, *hb, batch, out.orders);
+  s = finish_orders(e, *hb, batch->decode_orders, out.orders);
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[2], st));
   s = e->precision == HKB_PRECISION_FP32 ? decode_f32(e, *hb, db, eo, dt, out)
@@ -1153,6 +1154,145 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[3], st));
   HKB_CUDA(cudaGetLastError());
+  return kOk;
+}
+
+void record_timings(hkb_engine* e);
+
+// Teacher-forced scoring of an fp16 engine on tensor cores: the tensor-core
+// encoder, the per-residue decoder tables, then per decoder layer one slot
+// pass and one node pass over all (sequence, residue) rows.  `hb` holds the
+// validated batch; device inputs are uploaded here.
+hkb_status score_tc(hkb_engine* e, const hkb_score_batch* batch, HostBatch& hb,
+                    hkb_score_out* out) {
+  auto& ws = e->ws;
+  cudaStream_t st = e->stream;
+  const int64_t Q = hb.Q, R = hb.R;
+  e->launches = 0;
+  HKB_CUDA(cudaMemsetAsync(e->d_err, 0, sizeof(unsigned int), st));
+  float* d_coords = ws.get_as<float>("in.coords", R * 15);
+  uint8_t* d_src = ws.get_as<uint8_t>("in.src", R * 5);
+  int32_t* d_orders = ws.get_as<int32_t>("o.orders", Q);
+  int32_t* d_tok = ws.get_as<int32_t>("tf.tok", Q);
+  int* d_pos = ws.get_as<int>("tf.pos", Q);
+  int* d_rres = ws.get_as<int>("tf.rres", Q);
+  int* d_seq0 = ws.get_as<int>("tf.seq0", hb.B);
+  int* d_nseq = ws.get_as<int>("tf.nseq", hb.B);
+  float* S = ws.get_as<float>("tf.S", Q * kH);
+  float* h = ws.get_as<float>("tf.h", Q * kH);
+  float* A = ws.get_as<float>("tf.A", Q * kH);
+  uint16_t* PV = ws.get_as<uint16_t>("tf.PV", Q * kH);
+  float* LP = ws.get_as<float>("tf.LP", Q * kV);
+  float* sc = ws.get_as<float>("tf.sc", hb.NS);
+  if (!d_coords || !d_src || !d_orders || !d_tok || !d_pos || !d_rres || !d_seq0 || !d_nseq ||
+      !S || !h || !A || !PV || !LP || !sc)
+    return {HKB_UNAVAILABLE, "device allocation failed"};
+  HKB_CUDA(cudaMemcpyAsync(d_coords, batch->coords, sizeof(float) * R * 15,
+                           cudaMemcpyHostToDevice, st));
+  HKB_CUDA(cudaMemcpyAsync(d_src, batch->atom_sources, R * 5, cudaMemcpyHostToDevice, st));
+  HKB_CUDA(cudaMemcpyAsync(d_tok, batch->tokens, sizeof(int32_t) * Q, cudaMemcpyHostToDevice, st));
+  HKB_CUDA(cudaMemcpyAsync(d_seq0, hb.seq_base.data(), sizeof(int) * hb.B, cudaMemcpyHostToDevice,
+                           st));
+  HKB_CUDA(cudaMemcpyAsync(d_nseq, hb.S.data(), sizeof(int) * hb.B, cudaMemcpyHostToDevice, st));
+  DeviceBatch db;
+  db.coords = d_coords;
+  db.sources = d_src;
+  hkb_status s = upload_tables(e, hb, &db);
+  if (s.code != HKB_OK) return s;
+  HKB_CUDA(cudaEventRecord(e->ev[0], st));
+  if (batch->orders) {
+    HKB_CUDA(cudaMemcpyAsync(d_orders, batch->orders, sizeof(int32_t) * Q,
+                             cudaMemcpyHostToDevice, st));
+  } else {
+    s = launch_orders(e, hb, nullptr, nullptr, db, d_orders);
+    if (s.code != HKB_OK) return s;
+  }
+  EncoderOut eo;
+  s = encode_tc(e, hb, db, &eo);
+  if (s.code != HKB_OK) return s;
+  HKB_CUDA(cudaEventRecord(e->ev[1], st));
+  Bf16DecodeTables tb{};
+  s = decoder_tables_tc(e, hb, eo, &tb, /*with_pe=*/false);
+  if (s.code != HKB_OK) return s;
+  if (!batch->orders) {
+    s = finish_orders(e, hb, nullptr, d_orders);
+    if (s.code != HKB_OK) return s;
+  }
+  launch_tf_rows(st, db.bv, d_orders, d_pos, d_rres, e->d_err);
+  e->launches += 1;
+  HKB_CUDA(cudaEventRecord(e->ev[2], st));
+  const F32Weights& w = e->w32;
+  for (int l = 0; l < 3; ++l) {
+    const std::string q = "dec" + std::to_string(l) + ".";
+    // decode weight-stream tile of layer l: [W1a, W1d,] W2, W3, 4 x (W_in, W_out)
+    auto tile = [](int layer, int i) { return (layer == 0 ? 0 : 10 + 12 * (layer - 1) + 2) + i; };
+    TfSlotArgs sa;
+    sa.bv = db.bv;
+    sa.prot_seq0 = d_seq0;
+    sa.prot_nseq = d_nseq;
+    sa.layer = l;
+    sa.h_e = eo.h_e16;
+    sa.e_idx = eo.e_idx;
+    sa.pos = d_pos;
+    sa.tokens = d_tok;
+    sa.Aenc0 = tb.Aenc0;
+    sa.PVenc = tb.PVenc[l];
+    sa.A = A;
+    sa.PV = PV;
+    sa.Stab = w.dec[l].Stab;
+    sa.W1b = e->gemm_img.at(q + "W1b");
+    sa.W2 = static_cast<const unsigned char*>(e->d_stream) + (size_t)tile(l, 0) * kTileBytes;
+    sa.b2 = w.dec[l].b2;
+    sa.S = S;
+    sa.err = e->d_err;
+    launch_tf_slot_tc(st, sa, e->num_sms);
+    TfNodeArgs na;
+    na.bv = db.bv;
+    na.rows = Q;
+    na.layer = l;
+    na.row_res = d_rres;
+    na.mask = eo.mask;
+    na.h_enc = eo.h_v;
+    na.h = h;
+    na.S = S;
+    na.stream = static_cast<const unsigned char*>(e->d_stream);
+    na.tile_ids[0] = tile(l, 1);   // W3
+    for (int i = 0; i < 8; ++i) na.tile_ids[1 + i] = tile(l, 2 + i);
+    if (l < 2) {
+      na.tile_ids[9] = 10 + 12 * l;        // W1a of layer l+1
+      na.tile_ids[10] = 10 + 12 * l + 1;   // W1d of layer l+1
+      na.b1_next = w.dec[l + 1].b1;
+      na.A_next = A;
+      na.PV_next = PV;
+    }
+    const auto& D = w.dec[l];
+    na.b3 = D.b3;
+    na.n1w = D.n1w;
+    na.n1b = D.n1b;
+    na.bin = D.bin;
+    na.bout = D.bout;
+    na.n2w = D.n2w;
+    na.n2b = D.n2b;
+    na.headT = w.headT;
+    na.head_b = w.head_b;
+    na.log_probs = LP;
+    na.err = e->d_err;
+    launch_tf_node_tc(st, na, e->num_sms);
+    e->launches += 2;
+  }
+  launch_scores(st, db.bv, d_tok, LP, eo.mask, sc);
+  e->launches += 1;
+  HKB_CUDA(cudaEventRecord(e->ev[3], st));
+  HKB_CUDA(cudaGetLastError());
+  HKB_CUDA(cudaMemcpyAsync(out->log_probs, LP, sizeof(float) * Q * kV, cudaMemcpyDeviceToHost, st));
+  if (out->orders)
+    HKB_CUDA(cudaMemcpyAsync(out->orders, d_orders, sizeof(int32_t) * Q, cudaMemcpyDeviceToHost,
+                             st));
+  if (out->scores)
+    HKB_CUDA(cudaMemcpyAsync(out->scores, sc, sizeof(float) * hb.NS, cudaMemcpyDeviceToHost, st));
+  s = check_device_error(e);
+  if (s.code != HKB_OK) return s;
+  record_timings(e);
   return kOk;
 }
 
@@ -1424,6 +1564,13 @@ hkb_status hkb_mpnn_score(hkb_engine* e, const hkb_score_batch* batch, hkb_score
   for (int b = 0; b < hb.B; ++b)
     for (int q = 0; q < hb.S[b]; ++q)
       hb.seq_seed[hb.seq_base[b] + q] = (batch->seeds ? batch->seeds[b] : 0ull) + (uint64_t)q;
+  if (e->precision == HKB_PRECISION_F16) {
+    if (batch->orders)
+      for (int sq = 0; sq < hb.NS; ++sq)
+        if (!check_permutation(batch->orders + hb.seq_row_off[sq], hb.L[hb.seq_prot[sq]]))
+          return invalid("ProteinMPNN decoding_order must be a permutation");
+    return score_tc(e, batch, hb, out);
+  }
   if (batch->orders) {
     hb.orders.assign(batch->orders, batch->orders + hb.Q);
     for (int sq = 0; sq < hb.NS; ++sq)

@@ -279,6 +279,60 @@ struct DecTablesTcArgs {
 };
 void launch_dec_tables_tc(cudaStream_t st, const DecTablesTcArgs& p, int num_sms);
 
+// Teacher-forced pass on tensor cores (fp16 engines); rows are the [Q]
+// (sequence, residue) rows of the batch.
+struct TfSlotArgs {
+  BatchView bv;
+  const int* prot_seq0 = nullptr;       // [B] first sequence of protein b
+  const int* prot_nseq = nullptr;       // [B]
+  int layer = 0;
+  const uint16_t* h_e = nullptr;        // fp16 [R*48,128]
+  const int* e_idx = nullptr;           // [R,48]
+  const int* pos = nullptr;             // [Q] position of the row's residue in its order
+  const int* tokens = nullptr;          // [Q]
+  const float* Aenc0 = nullptr;         // [R,128] W1a_0 h_enc + b1_0 (layer 0)
+  const uint16_t* PVenc = nullptr;      // fp16 [R,128] W1d_l h_enc
+  const float* A = nullptr;             // [Q,128] W1a_l h + b1_l (layers 1, 2)
+  const uint16_t* PV = nullptr;         // fp16 [Q,128] W1d_l h (layers 1, 2)
+  const float* Stab = nullptr;          // [21,128] W1c_l W_s
+  const unsigned char* W1b = nullptr;   // fp16 SW128 images [128 out x 128 in]
+  const unsigned char* W2 = nullptr;
+  const float* b2 = nullptr;
+  float* S = nullptr;                   // [Q,128] out: sum_k GELU(W2 g + b2)
+  unsigned int* err = nullptr;
+};
+void launch_tf_slot_tc(cudaStream_t st, const TfSlotArgs& p, int num_sms);
+
+struct TfNodeArgs {
+  BatchView bv;
+  int64_t rows = 0;                     // Q
+  int layer = 0;
+  const int* row_res = nullptr;         // [Q] global residue of the row
+  const float* mask = nullptr;          // [R]
+  const float* h_enc = nullptr;         // [R,128] layer-0 residual
+  float* h = nullptr;                   // [Q,128] residual in (layers 1, 2), h' out
+  const float* S = nullptr;             // [Q,128]
+  const unsigned char* stream = nullptr;  // decode weight tiles (kStreamTilesPerStep)
+  int tile_ids[11] = {};                // W3, (W_in i, W_out i) x 4, W1a', W1d'
+  const float* b3 = nullptr;
+  const float* n1w = nullptr;
+  const float* n1b = nullptr;
+  const float* bin = nullptr;           // [512]
+  const float* bout = nullptr;
+  const float* n2w = nullptr;
+  const float* n2b = nullptr;
+  const float* b1_next = nullptr;
+  float* A_next = nullptr;              // [Q,128]
+  uint16_t* PV_next = nullptr;          // fp16 [Q,128]
+  const float* headT = nullptr;         // [128,21] (last layer)
+  const float* head_b = nullptr;
+  float* log_probs = nullptr;           // [Q,21] unscaled (last layer)
+  unsigned int* err = nullptr;
+};
+void launch_tf_node_tc(cudaStream_t st, const TfNodeArgs& p, int num_sms);
+void launch_tf_rows(cudaStream_t st, const BatchView& bv, const int32_t* orders, int* pos,
+                    int* row_res, unsigned int* err);
+
 int ar_tc_group_size();
 // f32 -> fp16 (f16 = true) or bf16, round to nearest even.
 void convert_f32_to_16(cudaStream_t st, const float* src, uint16_t* dst, int64_t n, bool f16);

@@ -1,0 +1,644 @@
+// Teacher-forced scoring on tcgen05 tensor cores (fp16 operands, fp32
+// accumulation, LayerNorm and softmax): the parallel causally masked decoder
+// pass of run_teacher_forced_decoder (inverse_fold_scalar.cpp:575-663) over
+// every (sequence, residue) row at once.  Each of the three decoder layers is
+// two persistent kernels:
+//
+//   tf_slot_tc   one residue t per work item, all of its protein's sequences
+//     D1 = W1b h_E[t]                       M = 128 features, N = 48 slots
+//     G  = GELU(D1 + A_row + V_slot)        per row (sequence) and slot k
+//        V_slot = PV_l[s, j] + W1c W_s[tok_j]   if pos_s(j) < pos_s(t)
+//               = W1d h_enc[j]                  otherwise
+//     D2 = W2 G                             N = 48 slots x up to 4 rows
+//     S_row = sum_{k < K} GELU(D2 + b2)
+//   The W1b h_E term is computed once per residue and shared by its rows.
+//
+//   tf_node_tc   128 rows per tile (rows on TMEM lanes, weights as B)
+//     h1 = LN1(h + (W3 S + K b3) / 30)
+//     h' = LN2(h1 + W_out GELU(W_in h1 + b_in) + b_out) * m_t
+//     then the next layer's node terms A = W1a h' + b1 (fp32) and
+//     PV = W1d h' (fp16), or, after the last layer, the logits and their
+//     unscaled log-softmax (log_softmax_scalar.cpp:8-37).
+//   Weight tiles stream through a 3-slot shared-memory ring by bulk copies.
+//
+// The split W1 . [h_t | h_E | W_s tok_j | h_j] = W1a h_t + W1b h_E + W1c W_s
+// tok_j + W1d h_j and W3 after the slot sum are exact in real arithmetic
+// (the same restatement as the autoregressive kernel).  Every wait is bounded.
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "kernels.hpp"
+#include "tcgen05.cuh"
+
+namespace hkb {
+namespace {
+
+using namespace tc;
+
+constexpr int kTfThreads = 512;
+constexpr uint32_t kW128 = 128 * 128 * 2;
+
+__device__ __forceinline__ uint32_t idesc_h(int M, int N) {
+  return idesc_bf16(M, N) & ~((7u << 7) | (7u << 10));
+}
+
+__device__ __forceinline__ float h2f(uint16_t v) {
+  return __half2float(__ushort_as_half(v));
+}
+
+// ---------------------------------------------------------------------------
+// Slot kernel
+// ---------------------------------------------------------------------------
+constexpr int kSubRows = 4;                        // rows per W2 MMA
+constexpr uint32_t kSOffW1b = 0;
+constexpr uint32_t kSOffW2 = kW128;
+constexpr uint32_t kSOffE = 2 * kW128;             // 2 h_E tiles of 48 rows
+constexpr uint32_t kETileBytes = kK * 256;         // 12 KiB
+constexpr uint32_t kSOffG = kSOffE + 2 * kETileBytes;
+constexpr uint32_t kGBytes = kSubRows * kK * 256;  // 48 KiB
+constexpr uint32_t kSOffStab = kSOffG + kGBytes;   // fp32 [21,128]
+constexpr uint32_t kSOffCode = kSOffStab + kV * kH * 4;   // int [4][48]
+constexpr uint32_t kSOffJ = kSOffCode + kSubRows * kK * 4; // int [48] local neighbour
+constexpr uint32_t kSlotSmem = kSOffJ + kK * 4 + 1024;
+
+__device__ __forceinline__ void load_etile(unsigned char* tile, const uint16_t* h_e, int64_t row0,
+                                           int64_t row_end, int tid) {
+  for (int c = tid; c < kK * 16; c += kTfThreads) {
+    const int r = c >> 4, k8 = c & 15;
+    const int64_t gr = row0 + r;
+    const bool ok = gr < row_end;
+    cp_async16(tile + sw128_offset(r, k8 * 8, kK), h_e + (ok ? gr : 0) * kH + k8 * 8, ok);
+  }
+}
+
+__global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_constant__ TfSlotArgs p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  float* StabS = reinterpret_cast<float*>(sm + kSOffStab);
+  int (*code)[kK] = reinterpret_cast<int (*)[kK]>(sm + kSOffCode);
+  int* SJ = reinterpret_cast<int*>(sm + kSOffJ);
+  __shared__ uint64_t bar_w, bar_mma;
+  __shared__ uint32_t tmem_base;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, rho = warp >> 2;   // feature quadrant, row of the sub-tile
+  const int f = quad * 32 + lane;
+  const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+  const int R = p.bv.total_residues;
+  const int64_t SL = (int64_t)R * kK;
+  const int l = p.layer;
+
+  if (tid == 0) {
+    mbar_init(&bar_w, 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 256);
+    tmem_relinquish();
+  }
+  for (int e = tid; e < kV * kH; e += kTfThreads) StabS[e] = p.Stab[e];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_base;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar_w, 2 * kW128);
+    for (uint32_t o = 0; o < kW128; o += 16384u) {
+      bulk_g2s(sm + kSOffW1b + o, p.W1b + o, 16384u, &bar_w);
+      bulk_g2s(sm + kSOffW2 + o, p.W2 + o, 16384u, &bar_w);
+    }
+  }
+  bool ok = mbar_wait(&bar_w, 0, p.err);
+  uint32_t ph = 0;
+  const float b2 = p.b2[f];
+  const float2 b2p = make_float2(b2, b2);
+  const float2 halfc = make_float2(0.5f, 0.5f);
+
+  int r = blockIdx.x;
+  if (r < R) load_etile(sm + kSOffE, p.h_e, (int64_t)r * kK, SL, tid);
+  cp_async_commit();
+  for (int it = 0; r < R; r += gridDim.x, ++it) {
+    if (__syncthreads_or(!ok)) break;
+    const int buf = it & 1;
+    unsigned char* etile = sm + kSOffE + buf * kETileBytes;
+    const int b = p.bv.res_prot[r];
+    const int L = p.bv.prot_len[b];
+    const int K = L < kK ? L : kK;
+    const int off = p.bv.prot_res_off[b];
+    const int t = r - off;
+    const int seq0 = p.prot_seq0[b];
+    const int nseq = p.prot_nseq[b];
+    cp_async_wait_all();
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      mma_k128(tm, smem_u32(sm + kSOffW1b), smem_u32(etile), kK, idesc_h(128, kK), false);
+      mma_commit(&bar_mma);
+    }
+    // the next residue's h_E rows into the other buffer (last read by the
+    // previous item's D1 MMA, which completed before its epilogue)
+    const int rn = r + gridDim.x;
+    if (rn < R) load_etile(sm + kSOffE + (buf ^ 1) * kETileBytes, p.h_e, (int64_t)rn * kK, SL, tid);
+    cp_async_commit();
+    if (tid < kK) {
+      int j = -1;
+      if (tid < K) {
+        j = p.e_idx[(int64_t)r * kK + tid];
+        if (j < 0 || j >= L) {
+          atomicOr(p.err, kErrBadIndex);
+          j = -1;
+        }
+      }
+      SJ[tid] = j;
+    }
+    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+    ph ^= 1;
+    tc_fence_after();
+    float d1[kK];
+    tmem_ld48(tm + lane_base, d1);
+    __syncthreads();   // SJ visible
+    for (int s0 = 0; s0 < nseq; s0 += kSubRows) {
+      const int nrows = nseq - s0 < kSubRows ? nseq - s0 : kSubRows;
+      const int N = nrows * kK;
+      // slot codes: j | bw << 16 | tok << 17 (-1 for an empty slot)
+      if (tid < nrows * kK) {
+        const int rr = tid / kK, k = tid % kK;
+        const int64_t qs = p.bv.seq_row_off[seq0 + s0 + rr];
+        const int j = SJ[k];
+        int c = -1;
+        if (j >= 0) {
+          const int64_t qj = qs + j;
+          const bool bw = p.pos[qj] < p.pos[qs + t];
+          const int tok = p.tokens[qj];
+          c = j | (bw ? 1 << 16 : 0) | (tok << 17);
+        }
+        code[rr][k] = c;
+      }
+      __syncthreads();
+      unsigned char* G = sm + kSOffG;
+      int64_t q = -1;
+      if (rho < nrows) {
+        const int64_t qs = p.bv.seq_row_off[seq0 + s0 + rho];
+        q = qs + t;
+        const float a = l == 0 ? p.Aenc0[(int64_t)r * kH + f] : p.A[q * kH + f];
+#pragma unroll
+        for (int k = 0; k < kK; k += 2) {
+          float x[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int c = code[rho][k + u];
+            float v = 0.0f;
+            if (c >= 0) {
+              const int j = c & 0xFFFF;
+              if ((c >> 16) & 1) {
+                const float pv = l == 0 ? h2f(p.PVenc[(int64_t)(off + j) * kH + f])
+                                        : h2f(p.PV[(qs + j) * kH + f]);
+                v = pv + StabS[(c >> 17) * kH + f];
+              } else {
+                v = h2f(p.PVenc[(int64_t)(off + j) * kH + f]);
+              }
+            }
+            x[u] = d1[k + u] + a + v;
+          }
+          // the operand holds 2 GELU(x); the epilogue halves D2 (exact)
+          const float2 y = gelu2_tc_x2(make_float2(x[0], x[1]));
+          const int c0 = code[rho][k], c1 = code[rho][k + 1];
+          *reinterpret_cast<__half*>(G + sw128_offset(rho * kK + k, f, N)) =
+              __float2half_rn(c0 >= 0 ? y.x : 0.0f);
+          *reinterpret_cast<__half*>(G + sw128_offset(rho * kK + k + 1, f, N)) =
+              __float2half_rn(c1 >= 0 ? y.y : 0.0f);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        if (ok) mma_k128(tm + 64, smem_u32(sm + kSOffW2), smem_u32(G), N, idesc_h(128, N), false);
+        mma_commit(&bar_mma);
+      }
+      if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+      ph ^= 1;
+      tc_fence_after();
+      if (rho < nrows) {
+        float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+#pragma unroll
+        for (int k0 = 0; k0 < kK; k0 += 16) {
+          float v[16];
+          tmem_ld16(tm + lane_base + 64u + (uint32_t)(rho * kK + k0), v);
+#pragma unroll
+          for (int k = 0; k < 16; k += 2) {
+            float2 g = gelu2_tc_x2(__ffma2_rn(make_float2(v[k], v[k + 1]), halfc, b2p));
+            if (k0 + k >= K) g.x = 0.0f;
+            if (k0 + k + 1 >= K) g.y = 0.0f;
+            acc[(k >> 1) & 1] = __fadd2_rn(acc[(k >> 1) & 1], g);
+          }
+        }
+        p.S[q * kH + f] = 0.5f * ((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y));
+      }
+      tc_fence_before();
+      __syncthreads();   // G and the codes are rewritten by the next sub-tile
+    }
+  }
+  cp_async_wait_all();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, 256);
+}
+
+// ---------------------------------------------------------------------------
+// Node kernel
+// ---------------------------------------------------------------------------
+constexpr int kRing = 3;
+constexpr uint32_t kNOffRing = 0;                         // 3 x 32 KiB weight tiles
+constexpr uint32_t kNOffA = kRing * kW128;                // A operand [128 rows x 128]
+constexpr uint32_t kNOffF = kNOffA + kW128;               // 2 FFN operands
+constexpr uint32_t kNOffRed = kNOffF + 2 * kW128;         // float [2][4][128]
+constexpr uint32_t kNOffHead = kNOffRed + 2 * 4 * 128 * 4;   // fp32 [21][128]
+constexpr uint32_t kNodeSmem = kNOffHead + kV * kH * 4 + 1024;
+static_assert(kNodeSmem <= 227 * 1024, "node kernel shared memory");
+// logits partials [21][4][128] fp32 reuse the FFN operand buffers
+static_assert(kV * 4 * 128 * 4 <= 2 * kW128, "logit partials");
+
+// TMEM columns
+constexpr uint32_t kNColD = 0;      // W3 / W1a'
+constexpr uint32_t kNColIn = 128;   // 2 x W_in chunk (the second reused by W1d')
+constexpr uint32_t kNColOut = 384;  // W_out accumulator
+
+struct Ring {
+  int issued;
+  int used;
+  int total;
+};
+
+__device__ __forceinline__ void ring_issue(Ring& rg, unsigned char* sm, uint64_t* full,
+                                           const TfNodeArgs& p, int per_tile) {
+  while (rg.issued < rg.total && rg.issued < rg.used + kRing) {
+    const int slot = rg.issued % kRing;
+    const int tile = p.tile_ids[rg.issued % per_tile];
+    mbar_arrive_expect_tx(&full[slot], kW128);
+    bulk_g2s(sm + kNOffRing + slot * kW128, p.stream + (size_t)tile * kW128, kW128, &full[slot]);
+    ++rg.issued;
+  }
+}
+
+__device__ __forceinline__ uint32_t ring_wait(int j, unsigned char* sm, uint64_t* full,
+                                              unsigned int* err, bool& ok) {
+  const int slot = j % kRing;
+  if (!mbar_wait(&full[slot], (uint32_t)((j / kRing) & 1), err)) ok = false;
+  return smem_u32(sm + kNOffRing + slot * kW128);
+}
+
+// LayerNorm of a 128-wide row whose 32-column parts are held by the four
+// threads (column groups) of one TMEM lane: partial sums through shared
+// memory, combined in a fixed order.
+__device__ __forceinline__ void row_layer_norm(float (&x)[32], const float* g, const float* bb,
+                                               float (*red)[4][128], int cg, int row) {
+  float s = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 32; ++c) s += x[c];
+  red[0][cg][row] = s;
+  __syncthreads();
+  const float mean = ((red[0][0][row] + red[0][1][row]) + (red[0][2][row] + red[0][3][row])) *
+                     (1.0f / 128.0f);
+  float v = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    x[c] -= mean;
+    v += x[c] * x[c];
+  }
+  red[1][cg][row] = v;
+  __syncthreads();
+  const float var = ((red[1][0][row] + red[1][1][row]) + (red[1][2][row] + red[1][3][row])) *
+                    (1.0f / 128.0f);
+  const float inv = 1.0f / sqrtf(var + kLnEps);
+#pragma unroll
+  for (int c = 0; c < 32; ++c) x[c] = x[c] * inv * g[cg * 32 + c] + bb[cg * 32 + c];
+}
+
+// 32 fp32 values of one row as fp16 into a SW128 [128 rows x 128] operand.
+__device__ __forceinline__ void store_row16(unsigned char* op, const float (&x)[32], int row,
+                                            int cg) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 h = __floats2half2_rn(x[8 * u + 2 * i], x[8 * u + 2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(op + sw128_offset(row, cg * 32 + 8 * u, 128)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+__global__ void __launch_bounds__(kTfThreads, 1) tf_node_tc_kernel(const __grid_constant__ TfNodeArgs p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  float (*red)[4][128] = reinterpret_cast<float (*)[4][128]>(sm + kNOffRed);
+  float* HeadS = reinterpret_cast<float*>(sm + kNOffHead);
+  __shared__ uint64_t full[kRing];
+  __shared__ uint64_t bar_mma;
+  __shared__ uint32_t tmem_base;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, cg = warp >> 2;   // row quadrant, 32-column group
+  const int row = quad * 32 + lane;
+  const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+  const int64_t tiles = (p.rows + 127) / 128;
+  const bool last = p.layer == 2;
+  const int per_tile = last ? 9 : 11;
+  const uint32_t idesc = idesc_h(128, 128);
+
+  if (tid == 0) {
+    for (int i = 0; i < kRing; ++i) mbar_init(&full[i], 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (last)
+    for (int e = tid; e < kV * kH; e += kTfThreads) {
+      const int v = e / kH, ff = e % kH;
+      HeadS[e] = p.headT[ff * kV + v];
+    }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tmem_base;
+  int64_t my_tiles = 0;
+  if ((int64_t)blockIdx.x < tiles) my_tiles = (tiles - 1 - blockIdx.x) / gridDim.x + 1;
+  Ring rg{0, 0, (int)(my_tiles * per_tile)};
+  if (tid == 0) ring_issue(rg, sm, full, p, per_tile);
+  bool ok = true;
+  uint32_t ph = 0;
+  int j = 0;   // next weight tile to consume (same on all threads)
+  unsigned char* Aop = sm + kNOffA;
+
+  auto mma_wait = [&]() {
+    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+    ph ^= 1;
+    tc_fence_after();
+  };
+
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    if (__syncthreads_or(!ok)) break;
+    const int64_t q = t * 128 + row;
+    const bool valid = q < p.rows;
+    int res = 0, K = 0;
+    float m = 0.0f;
+    if (valid) {
+      res = p.row_res[q];
+      const int L = p.bv.prot_len[p.bv.res_prot[res]];
+      K = L < kK ? L : kK;
+      m = p.mask[res];
+    }
+    float x[32];
+    {
+      const float* hrow = p.layer == 0 ? p.h_enc + (int64_t)res * kH : p.h + q * kH;
+      const float4* h4 = reinterpret_cast<const float4*>(hrow + cg * 32);
+      const float4* s4 = reinterpret_cast<const float4*>(p.S + q * kH + cg * 32);
+      float sv[32];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 hv = valid ? h4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 svv = valid ? s4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[4 * i] = hv.x; x[4 * i + 1] = hv.y; x[4 * i + 2] = hv.z; x[4 * i + 3] = hv.w;
+        sv[4 * i] = svv.x; sv[4 * i + 1] = svv.y; sv[4 * i + 2] = svv.z; sv[4 * i + 3] = svv.w;
+      }
+      store_row16(Aop, sv, row, cg);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---- W3 after the slot sum, residual + LayerNorm 1 ----------------------
+    if (tid == 0) {
+      const uint32_t w = ring_wait(j, sm, full, p.err, ok);
+      tc_fence_after();
+      if (ok) mma_k128(tm + kNColD, smem_u32(Aop), w, 128, idesc, false);
+      mma_commit(&bar_mma);
+    }
+    ++j;
+    mma_wait();
+    if (tid == 0) {
+      rg.used = j;
+      ring_issue(rg, sm, full, p, per_tile);
+    }
+    {
+      float v[32];
+      tmem_ld32(tm + lane_base + kNColD + (uint32_t)(cg * 32), v);
+      const float Kf = (float)K;
+#pragma unroll
+      for (int c = 0; c < 32; ++c)
+        x[c] = x[c] + (v[c] + Kf * p.b3[cg * 32 + c]) * (1.0f / kMessageScale);
+    }
+    row_layer_norm(x, p.n1w, p.n1b, red, cg, row);   // x = h1
+    tc_fence_before();
+    store_row16(Aop, x, row, cg);   // W3's MMA has completed: the operand is free
+    fence_async_smem();
+    __syncthreads();
+    // ---- FFN: DO = sum_i W_out[:, i] GELU(W_in[i] h1 + b_in[i]) ------------
+    if (tid == 0) {
+      const uint32_t w = ring_wait(j, sm, full, p.err, ok);
+      tc_fence_after();
+      if (ok) mma_k128(tm + kNColIn, smem_u32(Aop), w, 128, idesc, false);
+      mma_commit(&bar_mma);
+    }
+    ++j;
+    mma_wait();
+    for (int i = 0; i < 4; ++i) {
+      unsigned char* F = sm + kNOffF + (i & 1) * kW128;
+      {
+        float v[32];
+        tmem_ld32(tm + lane_base + kNColIn + (uint32_t)((i & 1) * 128 + cg * 32), v);
+        float y[32];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float2 g = gelu_tc_x2(make_float2(v[c] + p.bin[i * 128 + cg * 32 + c],
+                                                  v[c + 1] + p.bin[i * 128 + cg * 32 + c + 1]));
+          y[c] = g.x;
+          y[c + 1] = g.y;
+        }
+        store_row16(F, y, row, cg);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        rg.used = j;   // W_in[i] (and every earlier tile) is consumed
+        ring_issue(rg, sm, full, p, per_tile);
+        uint32_t w = ring_wait(j, sm, full, p.err, ok);   // W_out[:, i]
+        tc_fence_after();
+        if (ok) mma_k128(tm + kNColOut, smem_u32(F), w, 128, idesc, i > 0);
+        if (i < 3) {
+          w = ring_wait(j + 1, sm, full, p.err, ok);      // W_in[i + 1]
+          tc_fence_after();
+          if (ok) mma_k128(tm + kNColIn + (uint32_t)(((i + 1) & 1) * 128), smem_u32(Aop), w, 128,
+                           idesc, false);
+        }
+        mma_commit(&bar_mma);
+      }
+      j += i < 3 ? 2 : 1;
+      mma_wait();
+    }
+    if (tid == 0) {
+      rg.used = j;
+      ring_issue(rg, sm, full, p, per_tile);
+    }
+    // ---- residual + LayerNorm 2, residue mask ------------------------------
+    {
+      float v[32];
+      tmem_ld32(tm + lane_base + kNColOut + (uint32_t)(cg * 32), v);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) x[c] = x[c] + v[c] + p.bout[cg * 32 + c];
+    }
+    row_layer_norm(x, p.n2w, p.n2b, red, cg, row);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) x[c] = (m == 1.0f) ? x[c] : x[c] * m;
+    tc_fence_before();
+    if (!last) {
+      // ---- the next layer's node terms: A = W1a h' + b1, PV = W1d h' -------
+      if (valid) {
+        float4* o = reinterpret_cast<float4*>(p.h + q * kH + cg * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          o[i] = make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+      }
+      store_row16(Aop, x, row, cg);
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        uint32_t w = ring_wait(j, sm, full, p.err, ok);
+        tc_fence_after();
+        if (ok) mma_k128(tm + kNColD, smem_u32(Aop), w, 128, idesc, false);
+        w = ring_wait(j + 1, sm, full, p.err, ok);
+        tc_fence_after();
+        if (ok) mma_k128(tm + kNColIn, smem_u32(Aop), w, 128, idesc, false);
+        mma_commit(&bar_mma);
+      }
+      j += 2;
+      mma_wait();
+      if (tid == 0) {
+        rg.used = j;
+        ring_issue(rg, sm, full, p, per_tile);
+      }
+      {
+        float v[32];
+        tmem_ld32(tm + lane_base + kNColD + (uint32_t)(cg * 32), v);
+        if (valid) {
+          float4* o = reinterpret_cast<float4*>(p.A_next + q * kH + cg * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            o[i] = make_float4(v[4 * i] + p.b1_next[cg * 32 + 4 * i],
+                               v[4 * i + 1] + p.b1_next[cg * 32 + 4 * i + 1],
+                               v[4 * i + 2] + p.b1_next[cg * 32 + 4 * i + 2],
+                               v[4 * i + 3] + p.b1_next[cg * 32 + 4 * i + 3]);
+        }
+        tmem_ld32(tm + lane_base + kNColIn + (uint32_t)(cg * 32), v);
+        if (valid) {
+          uint4* o = reinterpret_cast<uint4*>(p.PV_next + q * kH + cg * 32);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const __half2 h = __floats2half2_rn(v[8 * u + 2 * i], v[8 * u + 2 * i + 1]);
+              w[i] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            o[u] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+      tc_fence_before();
+    } else {
+      // ---- logits (fp32) and the unscaled log-softmax -----------------------
+      float (*part)[4][128] = reinterpret_cast<float (*)[4][128]>(sm + kNOffF);
+#pragma unroll 1
+      for (int v = 0; v < kV; ++v) {
+        const float* hw = HeadS + v * kH + cg * 32;
+        float z = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) z = fmaf(x[c], hw[c], z);
+        part[v][cg][row] = z;
+      }
+      __syncthreads();
+      if (cg == 0 && valid) {
+        float z[kV], mx = -INFINITY;
+#pragma unroll
+        for (int v = 0; v < kV; ++v) {
+          z[v] = p.head_b[v] + ((part[v][0][row] + part[v][1][row]) +
+                                (part[v][2][row] + part[v][3][row]));
+          mx = fmaxf(mx, z[v]);
+        }
+        float sum = 0.0f;
+#pragma unroll
+        for (int v = 0; v < kV; ++v) sum += expf(z[v] - mx);
+        const float ls = logf(sum);
+        float* out = p.log_probs + q * kV;
+#pragma unroll
+        for (int v = 0; v < kV; ++v) out[v] = (z[v] - mx) - ls;
+      }
+    }
+  }
+  // Drain: no bulk copy may still be in flight when the CTA exits.
+  if (tid == 0)
+    for (int jj = j; jj < rg.issued; ++jj) {
+      const int slot = jj % kRing;
+      mbar_wait(&full[slot], (uint32_t)((jj / kRing) & 1), p.err);
+    }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tm, 512);
+}
+
+// pos[row of residue order[p]] = p and row -> residue, one CTA per sequence.
+__global__ void tf_rows_kernel(BatchView bv, const int32_t* __restrict__ orders,
+                               int* __restrict__ pos, int* __restrict__ row_res,
+                               unsigned int* err) {
+  const int sq = blockIdx.x;
+  const int b = bv.seq_prot[sq];
+  const int L = bv.prot_len[b];
+  const int off = bv.prot_res_off[b];
+  const int64_t q0 = bv.seq_row_off[sq];
+  for (int i = threadIdx.x; i < L; i += blockDim.x) {
+    const int t = orders[q0 + i];
+    if (t < 0 || t >= L) {
+      atomicOr(err, kErrBadIndex);
+    } else {
+      pos[q0 + t] = i;
+    }
+    row_res[q0 + i] = off + i;
+  }
+}
+
+}  // namespace
+
+void launch_tf_rows(cudaStream_t st, const BatchView& bv, const int32_t* orders, int* pos,
+                    int* row_res, unsigned int* err) {
+  if (bv.num_sequences <= 0) return;
+  tf_rows_kernel<<<bv.num_sequences, 256, 0, st>>>(bv, orders, pos, row_res, err);
+}
+
+void launch_tf_slot_tc(cudaStream_t st, const TfSlotArgs& p, int num_sms) {
+  const int R = p.bv.total_residues;
+  if (R <= 0) return;
+  ensure_dynamic_smem((const void*)tf_slot_tc_kernel, (int)kSlotSmem);
+  const int grid = R < num_sms ? R : num_sms;
+  tf_slot_tc_kernel<<<grid, kTfThreads, kSlotSmem, st>>>(p);
+}
+
+void launch_tf_node_tc(cudaStream_t st, const TfNodeArgs& p, int num_sms) {
+  const int64_t tiles = (p.rows + 127) / 128;
+  if (tiles <= 0) return;
+  ensure_dynamic_smem((const void*)tf_node_tc_kernel, (int)kNodeSmem);
+  const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+  tf_node_tc_kernel<<<grid, kTfThreads, kNodeSmem, st>>>(p);
+}
+
+}  // namespace hkb
