@@ -414,6 +414,372 @@ def run_ours(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# teacher-forced scoring, 128 x L=384 x 16 random sequences
+# ---------------------------------------------------------------------------
+C4_PROT, C4_L, C4_SEQ = 128, 384, 16
+METRIC4 = "ProteinMPNN v48 teacher-forced scored residues/sec at 128 x L=384 x 16 seqs"
+
+
+def config4_inputs(rank: int, synth):
+    """Backbone i of rank r: generator seed 3000 + 128 r + i; tokens uniform
+    over the 20 amino acids from numpy's default_rng(3 + r); random decoding
+    order per sequence from seed 3 + s."""
+    bb = [synth(3000 + C4_PROT * rank + i, C4_L) for i in range(C4_PROT)]
+    rng = np.random.default_rng(3 + rank)
+    toks = [rng.integers(0, 20, (C4_SEQ, C4_L)).astype(np.int32) for _ in range(C4_PROT)]
+    return [b[0] for b in bb], [b[1] for b in bb], toks
+
+
+def cpu_baseline_config4(threads: int):
+    """The reference's teacher-forced forward (compiled from its sources), one
+    config-4 sequence per host thread."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle.oracle import RefLib
+    ref = RefLib(WEIGHTS)
+    cs, ss, toks = config4_inputs(0, ref.synthetic_backbone)
+
+    def one(i):
+        b = i % C4_PROT
+        ref.teacher_forced(cs[b], ss[b], toks[b][i % C4_SEQ], None, seed=3 + i % C4_SEQ)
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(one, range(threads)))
+    dt = time.perf_counter() - t0
+    res = threads * C4_L
+    desc = (f"{threads} threads x 1 sequence of L=384 (config-4 backbones and tokens, random "
+            f"order) through the reference teacher-forced forward: {res} residues in {dt:.2f} s")
+    return res / dt, desc
+
+
+def run_config4(args):
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        cores = host_cores()
+        for _ in range(args.warmup):
+            cpu_baseline_config4(cores)
+        vals, desc = [], ""
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            v, desc = cpu_baseline_config4(cores)
+            vals.append(v)
+        value = float(np.mean(vals))
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC4, "value": value, "unit": "residues/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": (time.perf_counter() - t0) * 1000 / max(1, args.steps),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "config4 sample"},
+            "cpu_baseline": {"value": value, "unit": "residues/s", "cores": cores,
+                             "kind": "reference", "sample": desc},
+            "e2e": {"value": value, "unit": "residues/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return 0
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from hikoboshi_b200 import DesignEngine, synthetic_backbone
+    eng = DesignEngine(WEIGHTS, device=local, precision=args.precision)
+    cs, ss, toks = config4_inputs(rank, synthetic_backbone)
+    Q = C4_PROT * C4_SEQ * C4_L
+    flush = torch.empty(128 * 1024 * 1024, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def step():
+        eng.score(cs, ss, toks, seeds=3)
+
+    for _ in range(max(3, args.warmup)):
+        flush.zero_()
+        torch.cuda.synchronize(dev)
+        step()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    dev_ms, tf_ms, wall_ms, launches = [], [], [], 0
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        step()
+        wall_ms.append((time.perf_counter() - t0) * 1000)
+        tm = eng.last_timings()
+        dev_ms.append(tm["total_ms"])
+        tf_ms.append(tm["decode_ms"])
+        launches += eng.last_launch_count()
+    barrier()
+    clk = clocks.stop()
+    stats = torch.tensor([np.mean(dev_ms), np.mean(tf_ms), np.mean(wall_ms)], dtype=torch.float64,
+                         device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    d_ms, t_ms, w_ms = stats.tolist()
+    if rank == 0:
+        peaks, kind = measured_peaks()
+        achieved = FLOP_DECODE_PER_RES * Q / (t_ms / 1000) / 1e12
+        line = {
+            "metric": METRIC4, "value": Q * world / (d_ms / 1000), "unit": "residues/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": d_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": {"f16": "f16", "bf16": "bf16", "fp32": "f32"}[args.precision],
+            "data": "synthetic (seeded ideal-geometry backbones, uniform random tokens)",
+            "config": {"workload": "config4: teacher-forced scoring of 128 backbones x L=384 x 16 "
+                                   "sequences per GPU, random decoding order",
+                       "precision": args.precision,
+                       "l2": "flushed before every step (512 MiB write, outside the timing)",
+                       "timing": "value: device events around the pipeline (encoder, tables, "
+                                 "teacher-forced layers); e2e: the host call with uploads and "
+                                 "log-prob read-back"},
+            "tf_ms": t_ms,
+            "roofline": {"bound": "tensor", "kernel": "teacher-forced layers (tf_slot_tc + tf_node_tc)",
+                         "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                         "flops_per_launch": FLOP_DECODE_PER_RES * Q,
+                         "peak_kind": f"{kind} dense 16-bit tensor burst"},
+            "e2e": {"value": Q * world / (w_ms / 1000), "unit": "residues/s",
+                    "h2d_bytes_per_step": int(C4_PROT * C4_L * 20 + Q * 4),
+                    "d2h_bytes_per_step": int(Q * 21 * 4 + Q * 4 + C4_PROT * C4_SEQ * 4)},
+            "gpu_launches": int(launches / max(1, args.steps)),
+            "clocks": clk,
+        }
+        if not args.no_cpu_baseline:
+            cores = host_cores()
+            v, desc = cpu_baseline_config4(cores)
+            line["cpu_baseline"] = {"value": v, "unit": "residues/s", "cores": cores,
+                                    "kind": "reference", "sample": desc}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# BASELINE config 5: box-wide sweep, 4096 backbones L ~ U[64, 512] x 16 seqs
+# ---------------------------------------------------------------------------
+C5_PROT, C5_SEQ = 4096, 16
+METRIC5 = "ProteinMPNN v48 designed residues/sec box-wide, 4096 backbones L~U[64,512] x16 seqs"
+C5_CHUNK_RES = 4_194_304    # designed residues per device call (bounds device memory)
+
+
+def config5_lengths():
+    return [int(x) for x in np.random.default_rng(42).integers(64, 513, C5_PROT)]
+
+
+def config5_backbone(i: int, L: int, synth):
+    return synth(42_000 + i, L)
+
+
+def cpu_baseline_config5(threads: int):
+    """Stratified sample: one sequence per host thread, lengths at evenly
+    spaced quantiles of the config-5 length list; per-residue throughput of
+    the reference design path (the box-wide figure extrapolates it)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle.oracle import RefLib
+    ref = RefLib(WEIGHTS)
+    Ls = config5_lengths()
+    order = np.argsort(Ls, kind="stable")
+    pick = [int(order[int((k + 0.5) * C5_PROT / threads)]) for k in range(threads)]
+    inputs = [config5_backbone(i, Ls[i], ref.synthetic_backbone) for i in pick]
+
+    def one(k):
+        c, s = inputs[k]
+        ref.design(c, s, 1, seed=pick[k], temperature=TEMP, decode_order=0, keep_log_probs=False)
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(one, range(threads)))
+    dt = time.perf_counter() - t0
+    res = sum(Ls[i] for i in pick)
+    desc = (f"stratified sample: {threads} threads x 1 sequence, lengths at {threads} quantiles "
+            f"of the config-5 lengths ({res} residues in {dt:.2f} s); the box-wide value "
+            f"extrapolates this per-residue rate")
+    return res / dt, desc
+
+
+def run_config5(args):
+    import torch
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        cores = host_cores()
+        for _ in range(args.warmup):
+            cpu_baseline_config5(cores)
+        vals, desc = [], ""
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            v, desc = cpu_baseline_config5(cores)
+            vals.append(v)
+        value = float(np.mean(vals))
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC5, "value": value, "unit": "residues/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": (time.perf_counter() - t0) * 1000 / max(1, args.steps),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "config5 stratified sample"},
+            "cpu_baseline": {"value": value, "unit": "residues/s", "cores": cores,
+                             "kind": "reference", "sample": desc},
+            "e2e": {"value": value, "unit": "residues/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return 0
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import datetime
+    import torch.distributed as dist
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    from hikoboshi_b200 import DesignEngine, synthetic_backbone
+    from hikoboshi_b200 import _lib as hl
+    from hikoboshi_b200.shard import design_sharded, partition_proteins
+    eng = DesignEngine(WEIGHTS, device=local, precision=args.precision)
+    Ls = config5_lengths()
+    mine = partition_proteins(Ls, C5_SEQ, world)[rank]
+    total_res = sum(Ls) * C5_SEQ
+    # device-resident inputs of this rank's proteins, in chunks of whole proteins
+    chunks, cur, cur_res = [], [], 0
+    for b in mine:
+        if cur and cur_res + Ls[b] * C5_SEQ > C5_CHUNK_RES:
+            chunks.append(cur)
+            cur, cur_res = [], 0
+        cur.append(b)
+        cur_res += Ls[b] * C5_SEQ
+    if cur:
+        chunks.append(cur)
+    P = ctypes.POINTER
+    calls = []
+    max_q = max((sum(Ls[b] for b in ch) * C5_SEQ for ch in chunks), default=1)
+    d_tok = torch.empty(max_q, dtype=torch.int32, device=dev)
+    d_lp = torch.empty(max_q * 21, dtype=torch.float32, device=dev)
+    d_ord = torch.empty(max_q, dtype=torch.int32, device=dev)
+    d_sc = torch.empty(max(1, max_q // 64), dtype=torch.float32, device=dev)
+    keep = []
+    for ch in chunks:
+        bb = [config5_backbone(b, Ls[b], synthetic_backbone) for b in ch]
+        dc = torch.from_numpy(np.concatenate([x[0] for x in bb])).to(dev)
+        ds = torch.from_numpy(np.concatenate([x[1] for x in bb])).to(dev)
+        L = np.array([Ls[b] for b in ch], np.int32)
+        S = np.full(len(ch), C5_SEQ, np.int32)
+        seeds = np.array(ch, np.uint64)
+        temps = np.full(len(ch), TEMP, np.float32)
+        modes = np.zeros(len(ch), np.int32)
+        keep += [dc, ds, L, S, seeds, temps, modes]
+        calls.append(hl.DesignBatch(len(ch), L.ctypes.data_as(P(ctypes.c_int32)),
+                                    ctypes.c_void_p(dc.data_ptr()), ctypes.c_void_p(ds.data_ptr()),
+                                    S.ctypes.data_as(P(ctypes.c_int32)),
+                                    seeds.ctypes.data_as(P(ctypes.c_uint64)),
+                                    temps.ctypes.data_as(P(ctypes.c_float)),
+                                    modes.ctypes.data_as(P(ctypes.c_int32)), None))
+    odev = hl.DesignOut(ctypes.c_void_p(d_tok.data_ptr()), ctypes.c_void_p(d_lp.data_ptr()),
+                        ctypes.c_void_p(d_ord.data_ptr()), ctypes.c_void_p(d_sc.data_ptr()))
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    flush = torch.empty(128 * 1024 * 1024, dtype=torch.float32, device=dev)
+
+    def device_step():
+        for bt in calls:
+            hl.check(hl.load().hkb_mpnn_design_device(eng._h, ctypes.byref(bt), ctypes.byref(odev),
+                                                      ctypes.c_void_p(stream.cuda_stream)))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    steps = max(1, args.steps)
+    for _ in range(max(3, args.warmup)):
+        flush.zero_()
+        device_step()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    step_ms = []
+    for _ in range(steps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        device_step()
+        e1.record(stream)
+        e1.synchronize()
+        step_ms.append(e0.elapsed_time(e1))
+    barrier()
+    clk = clocks.stop()
+    # end to end: the sharded host API (every rank passes the whole batch,
+    # designs its partition, rank 0 gathers tokens, orders and scores)
+    allbb = [config5_backbone(b, Ls[b], synthetic_backbone) for b in range(C5_PROT)]
+    coords, sources = [x[0] for x in allbb], [x[1] for x in allbb]
+
+    def host_step():
+        return design_sharded(eng, coords, sources, C5_SEQ, seeds=list(range(C5_PROT)),
+                              temperatures=TEMP, keep_log_probs=False,
+                              max_rows_per_call=C5_CHUNK_RES)
+
+    host_step()
+    barrier()
+    e2e_steps = max(1, min(steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        host_step()
+    barrier()
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    stats = torch.tensor([float(np.mean(step_ms))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    step_s = stats.item() / 1000
+    if rank == 0:
+        peaks, kind = measured_peaks()
+        flops = FLOP_DECODE_PER_RES * total_res + FLOP_ENCODE_PER_RES * sum(Ls)
+        achieved = flops / step_s / 1e12
+        line = {
+            "metric": METRIC5, "value": total_res / step_s, "unit": "residues/s",
+            "n_gpus": world, "steps": steps, "warmup": max(3, args.warmup),
+            "ms_per_step": step_s * 1000, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": {"f16": "f16", "bf16": "bf16", "fp32": "f32"}[args.precision],
+            "data": "synthetic (seeded ideal-geometry backbones, lengths from default_rng(42))",
+            "config": {"workload": "config5: 4096 backbones, L uniform in [64, 512], 16 seqs each, "
+                                   "T=0.1, length-bucketed LPT partition by protein over the ranks",
+                       "designed_residues": total_res, "precision": args.precision,
+                       "l2": "flushed before every step (512 MiB write)",
+                       "device_calls_per_rank": len(calls)},
+            "per_gpu_residues_per_s": total_res / step_s / world,
+            "roofline": {"bound": "tensor", "kernel": "whole design step (encoder + decode)",
+                         "achieved": achieved, "peak": peaks["bf16_tflops"] * world,
+                         "unit": "TFLOP/s", "frac": achieved / (peaks["bf16_tflops"] * world),
+                         "traffic": None, "flops_per_launch": flops,
+                         "peak_kind": f"{kind} dense 16-bit tensor burst x {world} GPUs"},
+            "e2e": {"value": total_res / e2e_s, "unit": "residues/s",
+                    "h2d_bytes_per_step": int(sum(Ls) * 80),
+                    "d2h_bytes_per_step": int(total_res * 8 + C5_PROT * C5_SEQ * 4)},
+            "clocks": clk,
+        }
+        if not args.no_cpu_baseline:
+            cores = host_cores()
+            v, desc = cpu_baseline_config5(cores)
+            line["cpu_baseline"] = {"value": v, "unit": "residues/s", "cores": cores,
+                                    "kind": "reference", "sample": desc}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_profile_case(args):
     """One untimed design on a smaller case (64 backbones x L=128 x 32
     sequences, T=0.1) for ncu captures: the same kernels as the bench step
@@ -437,11 +803,18 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", choices=["f16", "bf16", "fp32"], default="f16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["config2", "config4", "config5"], default="config2",
+                    help="config2 (default): batched design; config4: teacher-forced scoring; "
+                         "config5: the mixed-length sweep sharded over the ranks")
     ap.add_argument("--profile-case", action="store_true",
                     help="one untimed design on 64 x L=128 x 32 (for ncu captures)")
     args = ap.parse_args()
     if args.profile_case:
         return run_profile_case(args)
+    if args.workload == "config4":
+        return run_config4(args)
+    if args.workload == "config5":
+        return run_config5(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -62,6 +62,38 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// 32 consecutive h_E values of one row stored as fp16 (hi, the MMA operand)
+// and fp16 remainders (lo): hi + lo keeps about 22 significant bits of the
+// residual stream between the encoder layers.
+__device__ __forceinline__ void store_hi_lo(uint16_t* hi, uint16_t* lo, const float (&x)[32]) {
+  uint32_t ph[16], pl[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const __half2 h = __floats2half2_rn(x[2 * q], x[2 * q + 1]);
+    const float2 hf = __half22float2(h);
+    ph[q] = *reinterpret_cast<const uint32_t*>(&h);
+    const __half2 l = __floats2half2_rn(x[2 * q] - hf.x, x[2 * q + 1] - hf.y);
+    pl[q] = *reinterpret_cast<const uint32_t*>(&l);
+  }
+  uint4* dh = reinterpret_cast<uint4*>(hi);
+  uint4* dl = reinterpret_cast<uint4*>(lo);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    dh[u] = make_uint4(ph[4 * u], ph[4 * u + 1], ph[4 * u + 2], ph[4 * u + 3]);
+    dl[u] = make_uint4(pl[4 * u], pl[4 * u + 1], pl[4 * u + 2], pl[4 * u + 3]);
+  }
+}
+
+// fp16 pair of (a, b) or, with lo, of their remainders a - fp16(a), b - fp16(b)
+// (exact in fp32): an operand x = hi + lo applied by two MMAs into one
+// accumulator carries about twice the fp16 precision.
+__device__ __forceinline__ uint32_t pack_h2s(float a, float b, bool lo) {
+  if (!lo) return pack_h2(a, b);
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 hf = __half22float2(h);
+  return pack_h2(a - hf.x, b - hf.y);
+}
+
 __device__ __forceinline__ uint32_t idesc_f16(int M, int N) {
   return idesc_bf16(M, N) & ~((7u << 7) | (7u << 10));
 }
@@ -95,11 +127,12 @@ __device__ __forceinline__ void load_weights(unsigned char* dst, const unsigned 
 constexpr int kNodeRes = 4;
 constexpr int kNodeSlots = kNodeRes * kK;                  // 192
 constexpr uint32_t kNodeTileBytes = kNodeSlots * 256;      // 48 KiB
-constexpr uint32_t kNodeOffW = 0;                          // W1b, W2
-constexpr uint32_t kNodeOffB = 2 * kW128Bytes;             // 2 h_E tiles
-constexpr uint32_t kNodeOffG = kNodeOffB + 2 * kNodeTileBytes;
+constexpr uint32_t kNodeOffW = 0;                          // W1b, W2, W1b rem., W2 rem.
+constexpr uint32_t kNodeOffB = 4 * kW128Bytes;             // h_E tile
+constexpr uint32_t kNodeOffG = kNodeOffB + kNodeTileBytes;
 constexpr uint32_t kNodeOffJ = kNodeOffG + kNodeTileBytes; // int [192] rj, float [192] att
 constexpr uint32_t kNodeSmem = kNodeOffJ + 2 * kNodeSlots * 4 + 1024;
+static_assert(kNodeSmem <= 227 * 1024, "node kernel shared memory");
 
 __global__ void __launch_bounds__(kEncThreads, 1)
     enc_node_tc_kernel(EncNodeTcArgs p) {
@@ -132,8 +165,8 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   tc_fence_after();
   const uint32_t tm = tmem_base;
   if (tid == 0) {
-    const unsigned char* imgs[2] = {p.W1b, p.W2};
-    load_weights(sm + kNodeOffW, imgs, 2, &bar_w);
+    const unsigned char* imgs[4] = {p.W1b, p.W2, p.W1b_lo, p.W2_lo};
+    load_weights(sm + kNodeOffW, imgs, 4, &bar_w);
   }
   bool ok = true;
   if (!mbar_wait(&bar_w, 0, p.err)) ok = false;
@@ -146,24 +179,19 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   cp_async_commit();
   for (int it = 0; t < tiles; t += gridDim.x, ++it) {
     if (__syncthreads_or(!ok)) break;
-    const int buf = it & 1;
-    unsigned char* btile = sm + kNodeOffB + buf * kNodeTileBytes;
+    unsigned char* btile = sm + kNodeOffB;
     cp_async_wait_all();
     fence_async_smem();
     __syncthreads();
     if (tid == 0) {
+      // D1 = W1b h_E as (hi + remainder) h_E: two MMAs into one accumulator
       tc_fence_after();
       mma_k128(tm, smem_u32(sm + kNodeOffW), smem_u32(btile), kNodeSlots,
                idesc_f16(128, kNodeSlots), false);
+      mma_k128(tm, smem_u32(sm + kNodeOffW + 2 * kW128Bytes), smem_u32(btile), kNodeSlots,
+               idesc_f16(128, kNodeSlots), true);
       mma_commit(&bar_mma);
     }
-    // next tile's rows (its buffer was last read by the previous tile's MMA,
-    // which completed before that tile's epilogue)
-    const int tn = t + gridDim.x;
-    if (tn < tiles)
-      load_rows_async(sm + kNodeOffB + (buf ^ 1) * kNodeTileBytes, p.h_e,
-                      (int64_t)tn * kNodeSlots, SL, kNodeSlots, tid);
-    cp_async_commit();
     // neighbour rows and attention weights of this tile's slots
     if (tid < kNodeSlots) {
       const int r = t * kNodeRes + tid / kK, k = tid % kK;
@@ -186,6 +214,12 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
+    // The h_E tile is free once D1's MMAs have completed: the next tile's rows
+    // load during this tile's epilogues.
+    const int tn = t + gridDim.x;
+    if (tn < tiles)
+      load_rows_async(sm + kNodeOffB, p.h_e, (int64_t)tn * kNodeSlots, SL, kNodeSlots, tid);
+    cp_async_commit();
     // epilogue 1: G[slot][f] = GELU(D1 + N_i + N_j)  (16-bit stores, B layout),
     // 16 TMEM columns at a time
     const int r = t * kNodeRes + rho;
@@ -215,6 +249,8 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       tc_fence_after();
       mma_k128(tm, smem_u32(sm + kNodeOffW + kW128Bytes), smem_u32(G), kNodeSlots,
                idesc_f16(128, kNodeSlots), false);
+      mma_k128(tm, smem_u32(sm + kNodeOffW + 3 * kW128Bytes), smem_u32(G), kNodeSlots,
+               idesc_f16(128, kNodeSlots), true);
       mma_commit(&bar_mma);
     }
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
@@ -260,18 +296,22 @@ __global__ void __launch_bounds__(kEncThreads, 1)
 // Edge-update kernel: 128 slots per tile.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kEdgeTileBytes = 128 * 256;             // 32 KiB
+// W11b, W12, W13 stay resident; their fp16 remainders (W - hi) stream through
+// a 2-slot ring in the order the MMAs use them (W11b, W12, W13 per tile).
 constexpr uint32_t kEdgeOffW = 0;                          // W11b, W12, W13
-constexpr uint32_t kEdgeOffA = 3 * kW128Bytes;             // 2 h_E tiles
-constexpr uint32_t kEdgeOffG = kEdgeOffA + 2 * kEdgeTileBytes;
-constexpr uint32_t kEdgeOffRed = kEdgeOffG + kEdgeTileBytes;   // float [2][4][128]
-constexpr uint32_t kEdgeSmem = kEdgeOffRed + 2 * 4 * 128 * 4 + 1024;
+constexpr uint32_t kEdgeOffR = 3 * kW128Bytes;             // remainder ring, 2 slots
+constexpr uint32_t kEdgeOffA = kEdgeOffR + 2 * kW128Bytes; // h_E tile
+constexpr uint32_t kEdgeOffG = kEdgeOffA + kEdgeTileBytes;
+constexpr uint32_t kEdgeOffRed = kEdgeOffG;   // float [2][4][128], used when G is free
+constexpr uint32_t kEdgeSmem = kEdgeOffG + kEdgeTileBytes + 1024;
+static_assert(kEdgeSmem <= 227 * 1024, "edge kernel shared memory");
 
 __global__ void __launch_bounds__(kEncThreads, 1)
     enc_edge_tc_kernel(EncEdgeTcArgs p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float (*red)[4][128] = reinterpret_cast<float (*)[4][128]>(sm + kEdgeOffRed);
-  __shared__ uint64_t bar_w, bar_mma;
+  __shared__ uint64_t bar_w, bar_mma, bar_r[2];
   __shared__ uint32_t tmem_base;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -286,6 +326,8 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   if (tid == 0) {
     mbar_init(&bar_w, 1);
     mbar_init(&bar_mma, 1);
+    mbar_init(&bar_r[0], 1);
+    mbar_init(&bar_r[1], 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -296,9 +338,28 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tmem_base;
+  // remainder-ring state (thread 0): entry j is remainder j % 3 of this CTA's
+  // tile j / 3, in slot j % 2
+  const unsigned char* rem[3] = {p.W11b_lo, p.W12_lo, p.W13_lo};
+  const int64_t my_tiles =
+      (int64_t)blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int64_t r_total = my_tiles * 3;
+  auto rem_issue = [&](int64_t j) {
+    if (j >= r_total) return;
+    uint64_t* b = &bar_r[j & 1];
+    mbar_arrive_expect_tx(b, kW128Bytes);
+    for (uint32_t o = 0; o < kW128Bytes; o += 16384u)
+      bulk_g2s(sm + kEdgeOffR + (j & 1) * kW128Bytes + o, rem[j % 3] + o, 16384u, b);
+  };
+  auto rem_wait = [&](int64_t j, bool& okf) {
+    if (!mbar_wait(&bar_r[j & 1], (uint32_t)((j >> 1) & 1), p.err)) okf = false;
+    return smem_u32(sm + kEdgeOffR + (j & 1) * kW128Bytes);
+  };
   if (tid == 0) {
     const unsigned char* imgs[3] = {p.W11b, p.W12, p.W13};
     load_weights(sm + kEdgeOffW, imgs, 3, &bar_w);
+    rem_issue(0);
+    rem_issue(1);
   }
   bool ok = true;
   if (!mbar_wait(&bar_w, 0, p.err)) ok = false;
@@ -309,22 +370,22 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   int64_t t = blockIdx.x;
   if (t < tiles) load_rows_async(sm + kEdgeOffA, p.h_e, t * 128, SL, 128, tid);
   cp_async_commit();
-  for (int it = 0; t < tiles; t += gridDim.x, ++it) {
+  int64_t rj0 = 0;   // remainder entry of this tile's first MMA
+  for (int it = 0; t < tiles; t += gridDim.x, ++it, rj0 += 3) {
     if (__syncthreads_or(!ok)) break;
-    const int buf = it & 1;
-    unsigned char* atile = sm + kEdgeOffA + buf * kEdgeTileBytes;
+    unsigned char* atile = sm + kEdgeOffA;
     cp_async_wait_all();
     fence_async_smem();
     __syncthreads();
     if (tid == 0) {
+      // each weight as hi + remainder: two MMAs into one accumulator
       tc_fence_after();
       mma_k128(tm, smem_u32(atile), smem_u32(sm + kEdgeOffW), 128, idesc, false);
+      const uint32_t r = rem_wait(rj0, ok);
+      tc_fence_after();
+      mma_k128(tm, smem_u32(atile), r, 128, idesc, true);
       mma_commit(&bar_mma);
     }
-    const int64_t tn = t + gridDim.x;
-    if (tn < tiles)
-      load_rows_async(sm + kEdgeOffA + (buf ^ 1) * kEdgeTileBytes, p.h_e, tn * 128, SL, 128, tid);
-    cp_async_commit();
     // this thread's slot
     const int64_t s = t * 128 + row;
     int r = 0, rj = -1;
@@ -340,6 +401,14 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
+    // D1's MMAs are complete: the h_E tile and the first remainder slot are
+    // free, so the next tile's rows and the next remainder load meanwhile.
+    if (tid == 0) rem_issue(rj0 + 2);
+    {
+      const int64_t tn = t + gridDim.x;
+      if (tn < tiles) load_rows_async(atile, p.h_e, tn * 128, SL, 128, tid);
+      cp_async_commit();
+    }
     // epilogue 1: G = GELU(D1 + N_i + N_j) on this thread's 32 columns
     {
       float v[32];
@@ -373,11 +442,15 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     if (tid == 0) {
       tc_fence_after();
       mma_k128(tm + 128, smem_u32(G), smem_u32(sm + kEdgeOffW + kW128Bytes), 128, idesc, false);
+      const uint32_t r = rem_wait(rj0 + 1, ok);
+      tc_fence_after();
+      mma_k128(tm + 128, smem_u32(G), r, 128, idesc, true);
       mma_commit(&bar_mma);
     }
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
+    if (tid == 0) rem_issue(rj0 + 3);
     // epilogue 2: G = GELU(D2 + b12)   (G was consumed by the MMA above)
     {
       float v[32];
@@ -400,26 +473,36 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     if (tid == 0) {
       tc_fence_after();
       mma_k128(tm, smem_u32(G), smem_u32(sm + kEdgeOffW + 2 * kW128Bytes), 128, idesc, false);
+      const uint32_t r = rem_wait(rj0 + 2, ok);
+      tc_fence_after();
+      mma_k128(tm, smem_u32(G), r, 128, idesc, true);
       mma_commit(&bar_mma);
     }
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
+    if (tid == 0) rem_issue(rj0 + 4);
     // epilogue 3: x = h_E + D3 + b13, LayerNorm over the row's 128 features
     // (four 32-column parts held by warps quad, quad+4, quad+8, quad+12)
     {
       float x[32];
       tmem_ld32(tm + lane_base + (uint32_t)c0, x);
+      // the residual h_E row as its fp16 value plus fp16 remainder (the tile
+      // buffer already holds the next tile's rows; this row sits in L2)
+      const int64_t srow = (s < SL ? s : 0) * kH + c0;
+      const uint4* hrow = reinterpret_cast<const uint4*>(p.h_e + srow);
+      const uint4* lrow = reinterpret_cast<const uint4*>(p.h_e_lo + srow);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const uint4 hv = *reinterpret_cast<const uint4*>(atile + sw128_offset(row, c0 + 8 * u, 128));
-        const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+        const uint4 hv = hrow[u], lv = lrow[u];
+        const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w}, lw[4] = {lv.x, lv.y, lv.z, lv.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 h2 = __half22float2(*reinterpret_cast<const __half2*>(&hw[i]));
+          const float2 l2 = __half22float2(*reinterpret_cast<const __half2*>(&lw[i]));
           const int c = 8 * u + 2 * i;
-          x[c] += h2.x + p.b13[c0 + c];
-          x[c + 1] += h2.y + p.b13[c0 + c + 1];
+          x[c] += (h2.x + l2.x) + p.b13[c0 + c];
+          x[c + 1] += (h2.y + l2.y) + p.b13[c0 + c + 1];
         }
       }
       float sum = 0.0f;
@@ -441,22 +524,19 @@ __global__ void __launch_bounds__(kEncThreads, 1)
           (red[1][0][row] + red[1][1][row] + red[1][2][row] + red[1][3][row]) * (1.0f / 128.0f);
       const float inv = 1.0f / sqrtf(var + kLnEps);
       if (rj >= 0) {
-        uint32_t pk[16];
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const int c = c0 + 2 * q;
-          pk[q] = pack_h2(x[2 * q] * inv * p.n3w[c] + p.n3b[c],
-                          x[2 * q + 1] * inv * p.n3w[c + 1] + p.n3b[c + 1]);
-        }
-        uint4* dst = reinterpret_cast<uint4*>(p.h_e_out + s * kH + c0);
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        for (int q = 0; q < 32; ++q) x[q] = x[q] * inv * p.n3w[c0 + q] + p.n3b[c0 + q];
+        store_hi_lo(p.h_e_out + s * kH + c0, p.h_e_lo + s * kH + c0, x);
       }
     }
     tc_fence_before();
   }
   cp_async_wait_all();
+  // Drain: no bulk copy may be in flight when the CTA exits (entries issued
+  // but not consumed after an early exit).
+  if (tid == 0)
+    for (int64_t j = rj0; j < r_total && j < rj0 + 2; ++j)
+      mbar_wait(&bar_r[j & 1], (uint32_t)((j >> 1) & 1), p.err);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -484,7 +564,7 @@ constexpr uint32_t kFeatSmem = kFeatOffRed + 2 * 4 * 128 * 4 + 1024;
 // 16-byte chunks at local column `col` of the feature chunk.
 __device__ __forceinline__ void feat_pair_item(unsigned char* A, int row, int p, int col,
                                                const int* SR, const int* SJ,
-                                               const EncFeatTcArgs& a) {
+                                               const EncFeatTcArgs& a, bool lo) {
   uint32_t pk[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   const int r = SR[row], rj = SJ[row];
   if (rj >= 0) {
@@ -493,7 +573,8 @@ __device__ __forceinline__ void feat_pair_item(unsigned char* A, int row, int p,
       const float dist =
           pair_distance(a.coords + ((int64_t)r * 5 + ai) * 3, a.coords + ((int64_t)rj * 5 + aj) * 3);
 #pragma unroll
-      for (int f = 0; f < 8; ++f) pk[f] = pack_h2(rbf_fast(dist, 2 * f), rbf_fast(dist, 2 * f + 1));
+      for (int f = 0; f < 8; ++f)
+        pk[f] = pack_h2s(rbf_fast(dist, 2 * f), rbf_fast(dist, 2 * f + 1), lo);
     }
   }
   *reinterpret_cast<uint4*>(A + sw128_offset(row, col, 128)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -572,65 +653,74 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       SC[tid] = cls;
     }
     __syncthreads();
-    // chunk 1: positional block (columns 0-15) and pairs 0-14 (16-255)
-    for (int m = tid; m < 256 + 15 * 128; m += kEncThreads) {
-      if (m < 256) {
-        const int rw = m >> 1, h = (m & 1) * 8;
-        const int cls = SC[rw];
-        uint32_t pk[4] = {0, 0, 0, 0};
-        if (cls >= 0) {
+    // chunk 1: positional block (columns 0-15) and pairs 0-14 (16-255), as
+    // fp16 values (pass 0) and then their fp16 remainders (pass 1), each
+    // pass followed by its MMAs into the same accumulator
+    for (int pass = 0; pass < 2; ++pass) {
+      const bool lo = pass == 1;
+      for (int m = tid; m < 256 + 15 * 128; m += kEncThreads) {
+        if (m < 256) {
+          const int rw = m >> 1, h = (m & 1) * 8;
+          const int cls = SC[rw];
+          uint32_t pk[4] = {0, 0, 0, 0};
+          if (cls >= 0) {
 #pragma unroll
-          for (int d = 0; d < 4; ++d) {
-            const int d0 = h + 2 * d;
-            pk[d] = pack_h2(p.pos_w[d0 * kPosClasses + cls] + p.pos_b[d0],
-                            p.pos_w[(d0 + 1) * kPosClasses + cls] + p.pos_b[d0 + 1]);
+            for (int d = 0; d < 4; ++d) {
+              const int d0 = h + 2 * d;
+              pk[d] = pack_h2s(p.pos_w[d0 * kPosClasses + cls] + p.pos_b[d0],
+                               p.pos_w[(d0 + 1) * kPosClasses + cls] + p.pos_b[d0 + 1], lo);
+            }
           }
+          *reinterpret_cast<uint4*>(A + sw128_offset(rw, h, 128)) =
+              make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        } else {
+          const int q = m - 256, rw = q & 127, pr = q >> 7;
+          feat_pair_item(A, rw, pr, 16 + 16 * pr, SR, SJ, p, lo);
         }
-        *reinterpret_cast<uint4*>(A + sw128_offset(rw, h, 128)) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      } else {
-        const int q = m - 256, rw = q & 127, pr = q >> 7;
-        feat_pair_item(A, rw, pr, 16 + 16 * pr, SR, SJ, p);
       }
-    }
-    fence_async_smem();
-    __syncthreads();
-    if (tid == 0) {
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        for (int kk = 0; kk < 16; ++kk) {
+          const uint32_t o = (uint32_t)(kk >> 2) * kAtomBytes + (uint32_t)(kk & 3) * 32u;
+          mma_bf16(tm, sw128_desc(smem_u32(A) + o), sw128_desc(smem_u32(sm + kFeatOffWedge) + o),
+                   idesc, (kk > 0 || lo) ? 1u : 0u);
+        }
+        mma_commit(&bar_mma);
+      }
+      if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+      ph ^= 1;
       tc_fence_after();
-      for (int kk = 0; kk < 16; ++kk) {
-        const uint32_t o = (uint32_t)(kk >> 2) * kAtomBytes + (uint32_t)(kk & 3) * 32u;
-        mma_bf16(tm, sw128_desc(smem_u32(A) + o), sw128_desc(smem_u32(sm + kFeatOffWedge) + o),
-                 idesc, kk > 0 ? 1u : 0u);
-      }
-      mma_commit(&bar_mma);
     }
-    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
-    ph ^= 1;
-    tc_fence_after();
-    // chunk 2: pairs 15-24 (columns 256-415) and zero padding (416-447)
-    for (int m = tid; m < 10 * 128 + 4 * 128; m += kEncThreads) {
-      if (m < 10 * 128) {
-        const int rw = m & 127, pr = 15 + (m >> 7);
-        feat_pair_item(A, rw, pr, 16 + 16 * pr - 256, SR, SJ, p);
-      } else {
-        const int q = m - 10 * 128, rw = q >> 2, u = q & 3;
-        *reinterpret_cast<uint4*>(A + sw128_offset(rw, 160 + 8 * u, 128)) = make_uint4(0, 0, 0, 0);
+    // chunk 2: pairs 15-24 (columns 256-415) and zero padding (416-447), the
+    // same two passes
+    for (int pass = 0; pass < 2; ++pass) {
+      const bool lo = pass == 1;
+      for (int m = tid; m < 10 * 128 + 4 * 128; m += kEncThreads) {
+        if (m < 10 * 128) {
+          const int rw = m & 127, pr = 15 + (m >> 7);
+          feat_pair_item(A, rw, pr, 16 + 16 * pr - 256, SR, SJ, p, lo);
+        } else {
+          const int q = m - 10 * 128, rw = q >> 2, u = q & 3;
+          *reinterpret_cast<uint4*>(A + sw128_offset(rw, 160 + 8 * u, 128)) = make_uint4(0, 0, 0, 0);
+        }
       }
-    }
-    fence_async_smem();
-    __syncthreads();
-    if (tid == 0) {
+      fence_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        for (int kk = 0; kk < 12; ++kk) {
+          const uint32_t o = (uint32_t)(kk >> 2) * kAtomBytes + (uint32_t)(kk & 3) * 32u;
+          mma_bf16(tm, sw128_desc(smem_u32(A) + o),
+                   sw128_desc(smem_u32(sm + kFeatOffWedge) + 4 * kAtomBytes + o), idesc, 1u);
+        }
+        mma_commit(&bar_mma);
+      }
+      if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+      ph ^= 1;
       tc_fence_after();
-      for (int kk = 0; kk < 12; ++kk) {
-        const uint32_t o = (uint32_t)(kk >> 2) * kAtomBytes + (uint32_t)(kk & 3) * 32u;
-        mma_bf16(tm, sw128_desc(smem_u32(A) + o),
-                 sw128_desc(smem_u32(sm + kFeatOffWedge) + 4 * kAtomBytes + o), idesc, 1u);
-      }
-      mma_commit(&bar_mma);
     }
-    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
-    ph ^= 1;
-    tc_fence_after();
     // LayerNorm of the 128-wide edge row (four 32-column parts) -> fp16 operand
     {
       float x[32];
@@ -653,42 +743,39 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       const float var =
           (red[1][0][row] + red[1][1][row] + red[1][2][row] + red[1][3][row]) * (1.0f / 128.0f);
       const float inv = 1.0f / sqrtf(var + kLnEps);
-      uint32_t pk[16];
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const int c = c0 + 2 * q;
-        pk[q] = pack_h2(x[2 * q] * inv * p.ln_w[c] + p.ln_b[c],
-                        x[2 * q + 1] * inv * p.ln_w[c + 1] + p.ln_b[c + 1]);
+      for (int i = 0; i < 32; ++i) x[i] = x[i] * inv * p.ln_w[c0 + i] + p.ln_b[c0 + i];
+      // LN_e(E) as fp16 (pass 0), then its fp16 remainder (pass 1), each
+      // times W_e into one accumulator
+      for (int pass = 0; pass < 2; ++pass) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) pk[q] = pack_h2s(x[2 * q], x[2 * q + 1], pass == 1);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          *reinterpret_cast<uint4*>(A + sw128_offset(row, c0 + 8 * u, 128)) =
+              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+          tc_fence_after();
+          mma_k128(tm + 128, smem_u32(A), smem_u32(sm + kFeatOffWe), 128, idesc, pass == 1);
+          mma_commit(&bar_mma);
+        }
+        if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
+        ph ^= 1;
+        tc_fence_after();
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        *reinterpret_cast<uint4*>(A + sw128_offset(row, c0 + 8 * u, 128)) =
-            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
     }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      mma_k128(tm + 128, smem_u32(A), smem_u32(sm + kFeatOffWe), 128, idesc, false);
-      mma_commit(&bar_mma);
-    }
-    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
-    ph ^= 1;
-    tc_fence_after();
     {
       const int64_t s = t * 128 + row;
       float v[32];
       tmem_ld32(tm + lane_base + 128u + (uint32_t)c0, v);
       if (s < SL) {
-        uint32_t pk[16];
 #pragma unroll
-        for (int q = 0; q < 16; ++q)
-          pk[q] = pack_h2(v[2 * q] + p.We_b[c0 + 2 * q], v[2 * q + 1] + p.We_b[c0 + 2 * q + 1]);
-        uint4* dst = reinterpret_cast<uint4*>(p.h_e + s * kH + c0);
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        for (int q = 0; q < 32; ++q) v[q] += p.We_b[c0 + q];
+        store_hi_lo(p.h_e + s * kH + c0, p.h_e_lo + s * kH + c0, v);
       }
     }
     tc_fence_before();

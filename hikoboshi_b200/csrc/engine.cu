@@ -306,7 +306,8 @@ void resolve_f32(const Prepared& P, const float* base, F32Weights* w) {
 }
 
 // --------------------------------------------------------------------------
-// bf16 decode weight stream: 34 SW128 tile images in consumption order
+// 16-bit decode weight stream: kStreamTilesPerStep SW128 tile images in
+// consumption order
 // --------------------------------------------------------------------------
 uint16_t f2bf(float f) {
   uint32_t u;
@@ -341,11 +342,56 @@ uint16_t f2h(float f) {
   return (uint16_t)h;
 }
 
+// IEEE binary16 -> binary32 (exact).
+float half_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h >> 15) << 31;
+  uint32_t ex = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+  uint32_t bits;
+  if (ex == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {   // subnormal: renormalise
+      ex = 113;
+      while (!(man & 0x400u)) {
+        man <<= 1;
+        --ex;
+      }
+      bits = sign | (ex << 23) | ((man & 0x3FFu) << 13);
+    }
+  } else if (ex == 31) {
+    bits = sign | 0x7F800000u | (man << 13);
+  } else {
+    bits = sign | ((ex + 112) << 23) | (man << 13);
+  }
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+
+// bf16 -> fp32 (exact).
+float bf_to_float(uint16_t h) {
+  const uint32_t u = (uint32_t)h << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+// The 16-bit rounding of v, or (lo) the 16-bit rounding of its remainder
+// v - hi: W = hi + lo carries about twice the 16-bit precision, and a product
+// W x is formed as hi x + lo x by two MMAs into one fp32 accumulator.
+uint16_t to16(float v, bool f16, bool lo) {
+  const uint16_t hi = f16 ? f2h(v) : f2bf(v);
+  if (!lo) return hi;
+  const float r = v - (f16 ? half_to_float(hi) : bf_to_float(hi));   // exact in fp32
+  return f16 ? f2h(r) : f2bf(r);
+}
+
 bool g_tile_f16 = true;   // operand format of the tiles being appended
 
 // Image of the 128 x 128 block W[r0:r0+128, k0:k0+128] (W row-major with
 // leading dimension ld) in the SW128 K-major layout of tcgen05.cuh.
-void append_tile(std::vector<uint16_t>& img, const float* W, int ld, int r0, int k0) {
+void append_tile(std::vector<uint16_t>& img, const float* W, int ld, int r0, int k0,
+                 bool lo = false) {
   const size_t base = img.size();
   img.resize(base + 128 * 128);
   for (int r = 0; r < 128; ++r)
@@ -353,7 +399,7 @@ void append_tile(std::vector<uint16_t>& img, const float* W, int ld, int r0, int
       const int byte = (k >> 6) * 128 * 128 + (r >> 3) * 1024 + (r & 7) * 128 +
                        ((((k & 63) >> 3) ^ (r & 7)) << 4) + (k & 7) * 2;
       const float v = W[(size_t)(r0 + r) * ld + k0 + k];
-      img[base + byte / 2] = g_tile_f16 ? f2h(v) : f2bf(v);
+      img[base + byte / 2] = to16(v, g_tile_f16, lo);
     }
 }
 
@@ -380,8 +426,9 @@ bool build_stream_image(const std::map<std::string, TensorView>& t, bool f16,
     append_tile(*img, W2, 128, 0, 0);
     append_tile(*img, W3, 128, 0, 0);
     for (int i = 0; i < 4; ++i) {
-      append_tile(*img, Wi, 128, 128 * i, 0);   // W_in rows 128i..128i+127
-      append_tile(*img, Wo, 512, 0, 128 * i);   // W_out columns 128i..128i+127
+      append_tile(*img, Wi, 128, 128 * i, 0);         // W_in rows 128i..128i+127
+      append_tile(*img, Wi, 128, 128 * i, 0, true);   // and their remainder
+      append_tile(*img, Wo, 512, 0, 128 * i);         // W_out columns 128i..128i+127
     }
   }
   return img->size() == (size_t)kStreamTilesPerStep * 128 * 128;
@@ -390,7 +437,7 @@ bool build_stream_image(const std::map<std::string, TensorView>& t, bool f16,
 // fp16 GEMM image of rows [r0, r0+nrows) and columns [c0, c0+K) of W
 // (row-major, leading dimension ld): [Kp/64 atoms][nrows x 64] SW128.
 void append_gemm_image(std::vector<uint16_t>& img, const float* W, int ld, int r0, int nrows,
-                       int c0, int K) {
+                       int c0, int K, bool lo = false) {
   const int Kp = (K + 63) & ~63;
   const size_t base = img.size();
   img.resize(base + (size_t)nrows * Kp, 0);
@@ -399,7 +446,7 @@ void append_gemm_image(std::vector<uint16_t>& img, const float* W, int ld, int r
       const size_t byte = (size_t)(k >> 6) * nrows * 128 + (size_t)(r >> 3) * 1024 +
                           (size_t)(r & 7) * 128 + (size_t)((((k & 63) >> 3) ^ (r & 7)) << 4) +
                           (size_t)(k & 7) * 2;
-      img[base + byte / 2] = f2h(W[(size_t)(r0 + r) * ld + c0 + k]);
+      img[base + byte / 2] = to16(W[(size_t)(r0 + r) * ld + c0 + k], true, lo);
     }
 }
 
@@ -422,17 +469,22 @@ bool build_gemm_images(const std::map<std::string, TensorView>& t, std::vector<u
   for (int l = 0; l < 3; ++l) {
     const std::string p = "encoder_layers." + std::to_string(l) + ".";
     const std::string q = "enc" + std::to_string(l) + ".";
+    // each edge-wise encoder weight also as its remainder image (".lo")
     for (const char* nm : {"W1", "W11"}) {
       const float* W = get(p + nm + ".weight");
       if (!W) return false;
       mark(q + nm + "b");   // the h_E input block
       append_gemm_image(*img, W, 384, 0, 128, 128, 128);
+      mark(q + nm + "b.lo");
+      append_gemm_image(*img, W, 384, 0, 128, 128, 128, true);
     }
     for (const char* nm : {"W2", "W12", "W13"}) {
       const float* W = get(p + nm + ".weight");
       if (!W) return false;
       mark(q + nm);
       append_gemm_image(*img, W, 128, 0, 128, 0, 128);
+      mark(q + nm + ".lo");
+      append_gemm_image(*img, W, 128, 0, 128, 0, 128, true);
     }
   }
   for (int l = 0; l < 3; ++l) {
@@ -705,6 +757,7 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   eo->mask = ws.get_as<float>("e.mask", R);
   eo->h_e = nullptr;
   eo->h_e16 = ws.get_as<uint16_t>("e.he16", SL * kH);
+  eo->h_e16lo = ws.get_as<uint16_t>("e.he16lo", SL * kH);
   eo->h_v = ws.get_as<float>("e.hv", R * kH);
   float* NAC = ws.get_as<float>("e.nac", R * 256);
   float* Sv = ws.get_as<float>("e.S", R * kH);
@@ -713,7 +766,7 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   float* h1 = ws.get_as<float>("e.h1", R * kH);
   float* F = ws.get_as<float>("e.F", R * kFfn);
   float* Y = ws.get_as<float>("e.Y", R * kH);
-  if (!eo->e_idx || !eo->d2 || !eo->mask || !eo->h_e16 || !eo->h_v || !NAC || !Sv || !cnt ||
+  if (!eo->e_idx || !eo->d2 || !eo->mask || !eo->h_e16 || !eo->h_e16lo || !eo->h_v || !NAC || !Sv || !cnt ||
       !T3 || !h1 || !F || !Y)
     return {HKB_UNAVAILABLE, "device allocation failed"};
   const BatchView& bv = db.bv;
@@ -739,6 +792,7 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   fa.ln_b = w.norm_e_b;
   fa.We_b = w.We_b;
   fa.h_e = eo->h_e16;
+  fa.h_e_lo = eo->h_e16lo;
   fa.err = e->d_err;
   launch_enc_featurize_tc(st, fa, e->num_sms);
   e->launches += 2;
@@ -757,6 +811,8 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
     na.NAC = NAC;
     na.W1b = e->gemm_img.at(q + "W1b");
     na.W2 = e->gemm_img.at(q + "W2");
+    na.W1b_lo = e->gemm_img.at(q + "W1b.lo");
+    na.W2_lo = e->gemm_img.at(q + "W2.lo");
     na.b2 = E.b2;
     na.S = Sv;
     na.cnt = cnt;
@@ -773,11 +829,15 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
     ea.bv = bv;
     ea.h_e = eo->h_e16;
     ea.h_e_out = eo->h_e16;
+    ea.h_e_lo = eo->h_e16lo;
     ea.e_idx = eo->e_idx;
     ea.NAC = NAC;
     ea.W11b = e->gemm_img.at(q + "W11b");
     ea.W12 = e->gemm_img.at(q + "W12");
     ea.W13 = e->gemm_img.at(q + "W13");
+    ea.W11b_lo = e->gemm_img.at(q + "W11b.lo");
+    ea.W12_lo = e->gemm_img.at(q + "W12.lo");
+    ea.W13_lo = e->gemm_img.at(q + "W13.lo");
     ea.b12 = E.b12;
     ea.b13 = E.b13;
     ea.n3w = E.n3w;
@@ -1224,8 +1284,9 @@ hkb_status score_tc(hkb_engine* e, const hkb_score_batch* batch, HostBatch& hb,
   const F32Weights& w = e->w32;
   for (int l = 0; l < 3; ++l) {
     const std::string q = "dec" + std::to_string(l) + ".";
-    // decode weight-stream tile of layer l: [W1a, W1d,] W2, W3, 4 x (W_in, W_out)
-    auto tile = [](int layer, int i) { return (layer == 0 ? 0 : 10 + 12 * (layer - 1) + 2) + i; };
+    // decode weight-stream tile of layer l: [W1a, W1d,] W2, W3, then
+    // 4 x (W_in, W_in remainder, W_out)
+    auto tile = [](int layer, int i) { return stream_w2_tile(layer) + i; };
     TfSlotArgs sa;
     sa.bv = db.bv;
     sa.prot_seq0 = d_seq0;
@@ -1257,10 +1318,10 @@ hkb_status score_tc(hkb_engine* e, const hkb_score_batch* batch, HostBatch& hb,
     na.S = S;
     na.stream = static_cast<const unsigned char*>(e->d_stream);
     na.tile_ids[0] = tile(l, 1);   // W3
-    for (int i = 0; i < 8; ++i) na.tile_ids[1 + i] = tile(l, 2 + i);
+    for (int i = 0; i < 12; ++i) na.tile_ids[1 + i] = tile(l, 2 + i);
     if (l < 2) {
-      na.tile_ids[9] = 10 + 12 * l;        // W1a of layer l+1
-      na.tile_ids[10] = 10 + 12 * l + 1;   // W1d of layer l+1
+      na.tile_ids[13] = stream_w1a_tile(l + 1);       // W1a of layer l+1
+      na.tile_ids[14] = stream_w1a_tile(l + 1) + 1;   // W1d of layer l+1
       na.b1_next = w.dec[l + 1].b1;
       na.A_next = A;
       na.PV_next = PV;
@@ -1415,6 +1476,23 @@ hkb_status hkb_mpnn_create(const void* st_blob, size_t length, int device,
     }
     W.headT = e->w32.headT;
     W.head_b = e->w32.head_b;
+    // the decode kernel's logit head: [21][kHeadPitch] fp32, rows padded
+    auto it = tensors.find("W_out.weight");
+    if (it == tensors.end()) {
+      hkb_mpnn_destroy(e);
+      return invalid("ProteinMPNN v_48_020 weights: missing W_out.weight");
+    }
+    std::vector<float> hp((size_t)kV * kHeadPitch, 0.0f);
+    for (int v = 0; v < kV; ++v)
+      for (int f = 0; f < kH; ++f) hp[(size_t)v * kHeadPitch + f] = it->second.data[v * kH + f];
+    if (cudaMalloc(&e->d_head, hp.size() * sizeof(float)) != cudaSuccess ||
+        cudaMemcpy(e->d_head, hp.data(), hp.size() * sizeof(float), cudaMemcpyHostToDevice) !=
+            cudaSuccess) {
+      cudaGetLastError();
+      hkb_mpnn_destroy(e);
+      return {HKB_UNAVAILABLE, "device allocation failed"};
+    }
+    W.headP = static_cast<const float*>(e->d_head);
   }
   *out = e;
   return kOk;
@@ -1428,6 +1506,7 @@ void hkb_mpnn_destroy(hkb_engine* e) {
   if (e->d_weights) cudaFree(e->d_weights);
   if (e->d_stream) cudaFree(e->d_stream);
   if (e->d_gemm) cudaFree(e->d_gemm);
+  if (e->d_head) cudaFree(e->d_head);
   if (e->d_err) cudaFree(e->d_err);
   for (auto& ev : e->ev)
     if (ev) cudaEventDestroy(ev);
@@ -1746,31 +1825,6 @@ static hkb_status single_protein_encode(hkb_engine* e, int32_t L, const float* c
   return kOk;
 }
 
-// IEEE binary16 -> binary32 (exact).
-static float half_to_float(uint16_t h) {
-  const uint32_t sign = (uint32_t)(h >> 15) << 31;
-  uint32_t ex = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
-  uint32_t bits;
-  if (ex == 0) {
-    if (man == 0) {
-      bits = sign;
-    } else {   // subnormal: renormalise
-      ex = 113;
-      while (!(man & 0x400u)) {
-        man <<= 1;
-        --ex;
-      }
-      bits = sign | (ex << 23) | ((man & 0x3FFu) << 13);
-    }
-  } else if (ex == 31) {
-    bits = sign | 0x7F800000u | (man << 13);
-  } else {
-    bits = sign | ((ex + 112) << 23) | (man << 13);
-  }
-  float f;
-  std::memcpy(&f, &bits, 4);
-  return f;
-}
 
 static void compact_rows(const void* src, void* dst, int L, int K, size_t elem, size_t width) {
   // [L,48,width] -> [L,K,width]
@@ -1789,19 +1843,22 @@ hkb_status hkb_mpnn_encode(hkb_engine* e, int32_t L, const float* coords,
   if (s.code != HKB_OK) return s;
   const int K = std::min(L, kK);
   std::vector<float> he((size_t)L * kK * kH);
-  std::vector<uint16_t> he16(eo.h_e16 ? he.size() : 0);
+  std::vector<uint16_t> he16(eo.h_e16 ? he.size() : 0), he16lo(he16.size());
   std::vector<int> idx((size_t)L * kK);
   cudaStream_t st = e->stream;
   if (h_v) HKB_CUDA(cudaMemcpyAsync(h_v, eo.h_v, sizeof(float) * L * kH, cudaMemcpyDeviceToHost, st));
-  if (eo.h_e16)
+  if (eo.h_e16) {
     HKB_CUDA(cudaMemcpyAsync(he16.data(), eo.h_e16, he16.size() * sizeof(uint16_t),
                              cudaMemcpyDeviceToHost, st));
+    HKB_CUDA(cudaMemcpyAsync(he16lo.data(), eo.h_e16lo, he16lo.size() * sizeof(uint16_t),
+                             cudaMemcpyDeviceToHost, st));
+  }
   else
     HKB_CUDA(cudaMemcpyAsync(he.data(), eo.h_e, he.size() * sizeof(float), cudaMemcpyDeviceToHost, st));
   HKB_CUDA(cudaMemcpyAsync(idx.data(), eo.e_idx, idx.size() * sizeof(int), cudaMemcpyDeviceToHost, st));
   s = check_device_error(e);
   if (s.code != HKB_OK) return s;
-  for (size_t i = 0; i < he16.size(); ++i) he[i] = half_to_float(he16[i]);
+  for (size_t i = 0; i < he16.size(); ++i) he[i] = half_to_float(he16[i]) + half_to_float(he16lo[i]);
   if (h_e) compact_rows(he.data(), h_e, L, K, sizeof(float), kH);
   if (e_idx) compact_rows(idx.data(), e_idx, L, K, sizeof(int), 1);
   return kOk;

@@ -67,6 +67,7 @@ struct EncoderOut {
   float* mask = nullptr;  // [R]
   float* h_e = nullptr;   // [R,48,128] (fp32 encoder)
   uint16_t* h_e16 = nullptr;  // [R,48,128] fp16 (tensor-core encoder)
+  uint16_t* h_e16lo = nullptr;  // its fp16 remainder (h_E = hi + lo)
   float* h_v = nullptr;   // [R,128]
 };
 
@@ -82,6 +83,7 @@ struct hkb_engine {
   void* d_stream = nullptr;          // 16-bit decode weight tiles (SW128 images)
   hkb::Bf16DecodeWeights wbf{};
   void* d_gemm = nullptr;            // fp16 GEMM weight images (tensor-core modes)
+  void* d_head = nullptr;            // decode kernel's logit head [21][kHeadPitch]
   std::map<std::string, const unsigned char*> gemm_img;
   int num_sms = 148;
   hkb::Workspace ws;

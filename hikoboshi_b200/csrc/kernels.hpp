@@ -170,15 +170,29 @@ int ar_f32_group_size();
 
 // ---- bf16 tensor-core path --------------------------------------------------
 // Weight tiles for the fused decode kernel: every 128 x 128 operand tile is a
-// bf16 image already in the SW128 K-major shared-memory layout, and the tiles
-// sit in the exact order the kernel consumes them in one decode position:
-//   layer 0: W2, W3, (W_in[i], W_out[:, i]) for i = 0..3        (10 tiles)
-//   then for l = 1, 2: W1a_l, W1d_l, W2_l, W3_l, 4 x (W_in, W_out) (12 each)
-constexpr int kStreamTilesPerStep = 34;
+// 16-bit image already in the SW128 K-major shared-memory layout, and the
+// tiles sit in the exact order the kernel consumes them in one decode position:
+//   layer 0: W2, W3, (W_in[i], W_in[i] remainder, W_out[:, i]) for i = 0..3
+//                                                                 (14 tiles)
+//   then for l = 1, 2: W1a_l, W1d_l, W2_l, W3_l, 4 x (W_in, W_in rem., W_out)
+//                                                                 (16 each)
+// W_in is applied as hi + remainder (two MMAs into one accumulator): its
+// 16-bit rounding is the largest single error source of the decoder.
+constexpr int kStreamTilesPerStep = 46;
+// Stream tile index of layer l's W2 (its W1a and W1d sit just before it for
+// l > 0); W3 follows W2, then W_in[i] (hi, remainder) and W_out[:, i].
+__host__ __device__ constexpr int stream_w2_tile(int l) { return l == 0 ? 0 : 14 + 16 * (l - 1) + 2; }
+__host__ __device__ constexpr int stream_w1a_tile(int l) { return 14 + 16 * (l - 1); }
 constexpr int kTileBytes = 128 * 128 * 2;
 
+// Logit head of the decode kernel: fp32, transposed, one padded row per
+// vocabulary entry (a logit is a float4 walk along both operands; the 528-byte
+// pitch spreads eight consecutive entries over all 32 banks).
+constexpr int kHeadPitch = 128 + 4;
+
 struct Bf16DecodeWeights {
-  const unsigned char* stream;  // [34][32 KiB]
+  const unsigned char* stream;  // [kStreamTilesPerStep][32 KiB]
+  const float* headP = nullptr; // [21][kHeadPitch]
   const float* Stab[3];         // [21,128] W1c_l . W_s
   const float* b1[3];
   const float* b2[3];
@@ -226,6 +240,8 @@ struct EncNodeTcArgs {
   const float* NAC = nullptr;
   const unsigned char* W1b = nullptr;   // fp16 SW128 images [128 out x 128 in]
   const unsigned char* W2 = nullptr;
+  const unsigned char* W1b_lo = nullptr;   // their fp16 remainders (W - hi)
+  const unsigned char* W2_lo = nullptr;
   const float* b2 = nullptr;
   float* S = nullptr;                   // [R,128] masked slot sums of GELU(W2 g + b2)
   float* cnt = nullptr;                 // [R] sum of m_i m_j
@@ -237,11 +253,15 @@ struct EncEdgeTcArgs {
   BatchView bv;
   const uint16_t* h_e = nullptr;        // read
   uint16_t* h_e_out = nullptr;          // written on slots with a valid neighbour (may alias)
+  uint16_t* h_e_lo = nullptr;           // fp16 remainder of h_E (read and written in place)
   const int* e_idx = nullptr;
   const float* NAC = nullptr;           // [W11a h + b11 | W11c h]
   const unsigned char* W11b = nullptr;
   const unsigned char* W12 = nullptr;
   const unsigned char* W13 = nullptr;
+  const unsigned char* W11b_lo = nullptr;   // fp16 remainders (W - hi)
+  const unsigned char* W12_lo = nullptr;
+  const unsigned char* W13_lo = nullptr;
   const float* b12 = nullptr;
   const float* b13 = nullptr;
   const float* n3w = nullptr;
@@ -265,6 +285,7 @@ struct EncFeatTcArgs {
   const float* ln_b = nullptr;
   const float* We_b = nullptr;
   uint16_t* h_e = nullptr;
+  uint16_t* h_e_lo = nullptr;           // fp16 remainder of every h_E value
   unsigned int* err = nullptr;
 };
 void launch_enc_featurize_tc(cudaStream_t st, const EncFeatTcArgs& p, int num_sms);
@@ -313,7 +334,7 @@ struct TfNodeArgs {
   float* h = nullptr;                   // [Q,128] residual in (layers 1, 2), h' out
   const float* S = nullptr;             // [Q,128]
   const unsigned char* stream = nullptr;  // decode weight tiles (kStreamTilesPerStep)
-  int tile_ids[11] = {};                // W3, (W_in i, W_out i) x 4, W1a', W1d'
+  int tile_ids[15] = {};                // W3, (W_in i, W_in i rem., W_out i) x 4, W1a', W1d'
   const float* b3 = nullptr;
   const float* n1w = nullptr;
   const float* n1b = nullptr;

@@ -40,7 +40,7 @@ using namespace tc;
 constexpr int kGB = 16;           // sequences per CTA
 constexpr int kChunkSeqs = 2;     // sequences per message MMA
 constexpr int kChunkN = kChunkSeqs * kK;  // 96 neighbour slots
-constexpr int kSlots = 3;         // weight ring depth
+constexpr int kSlots = 4;         // weight ring depth
 constexpr int kThreadsB = 512;
 constexpr int kWarpsB = kThreadsB / 32;
 constexpr int kGroupThreads = 256;  // message-phase ping-pong group: warps 0-7 / 8-15
@@ -67,15 +67,13 @@ constexpr uint32_t kOffAa = kOffH + kGB * kH * 4;
 constexpr uint32_t kOffXs = kOffAa + kGB * kH * 4;
 constexpr uint32_t kOffNb = kOffXs + kGB * kH * 4;              // int [16,48]
 constexpr uint32_t kOffLogit = kOffNb + kGB * kK * 4;           // float [16,32]
-constexpr uint32_t kOffStab = kOffLogit + kGB * 32 * 4;         // 16-bit [3,21,128]
-constexpr uint32_t kOffHead = kOffStab + 16384;                 // fp32 [21][kHeadPitch]
-// Logit head stored transposed, one padded row per vocabulary entry: a logit
-// is a float4 walk along both operands, and the 528-byte pitch spreads eight
-// consecutive entries over all 32 banks.
-constexpr int kHeadPitch = kH + 4;
-constexpr uint32_t kOffNbNext = kOffHead + kV * kHeadPitch * 4; // int [16,48] next position
+// The W1c.W_s tables (fp32 [3][21][128]) and the logit head (fp32, transposed
+// with a padded pitch) are read from global memory through L1: shared memory
+// goes to the fourth weight-ring slot.
+constexpr uint32_t kOffNbNext = kOffLogit + kGB * 32 * 4;       // int [16,48] next position
 constexpr uint32_t kOffMisc = kOffNbNext + kGB * kK * 4;
 constexpr uint32_t kSmemBytes = kOffMisc + 1024 + 1024;         // + misc + alignment slack
+static_assert(kSmemBytes <= 227 * 1024, "decode kernel shared memory");
 
 struct Misc {
   uint64_t full[kSlots];
@@ -122,23 +120,6 @@ __device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
   }
 }
 
-// Element-wise a + b + c of eight fp16 values, in half2 pairs.
-template <bool F16>
-__device__ __forceinline__ uint4 add3_16(const uint4 a, const uint4 b, const uint4 c) {
-  static_assert(F16, "fp16 only");
-  const uint32_t x[4] = {a.x, a.y, a.z, a.w}, y[4] = {b.x, b.y, b.z, b.w},
-                 z[4] = {c.x, c.y, c.z, c.w};
-  uint32_t o[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __half2 r = __hadd2(__hadd2(*reinterpret_cast<const __half2*>(&x[i]),
-                                      *reinterpret_cast<const __half2*>(&y[i])),
-                              *reinterpret_cast<const __half2*>(&z[i]));
-    o[i] = *reinterpret_cast<const uint32_t*>(&r);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
 template <bool F16>
 __device__ __forceinline__ uint16_t to16(float a) {
   return (uint16_t)(pack16<F16>(a, 0.0f) & 0xFFFFu);
@@ -158,7 +139,7 @@ __device__ __forceinline__ unsigned long long splitmix_next(unsigned long long& 
 }
 
 // Thread-0 state of the weight-tile stream.  32-bit counters (at most
-// 4096 x 34 tiles): the slot and tile indices are taken modulo 3 and 34 on
+// 4096 x 46 tiles): the slot and tile indices are taken modulo 4 and 46 on
 // every issue, on thread 0's critical path, and 64-bit remainders cost
 // several times more.
 struct Stream {
@@ -204,8 +185,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   int (*Nb)[kK] = reinterpret_cast<int (*)[kK]>(sm + kOffNb);
   int (*NbNext)[kK] = reinterpret_cast<int (*)[kK]>(sm + kOffNbNext);
   float (*Lg)[32] = reinterpret_cast<float (*)[32]>(sm + kOffLogit);
-  uint16_t* StabS = reinterpret_cast<uint16_t*>(sm + kOffStab);
-  float* HeadS = reinterpret_cast<float*>(sm + kOffHead);
+  const float* HeadS = w.headP;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -243,15 +223,6 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   // Zero the small operand tiles once (rows of absent sequences stay zero).
   for (int e = tid; e < 4 * 4096 / 16; e += kThreadsB)
     reinterpret_cast<uint4*>(sm + kOffHb)[e] = make_uint4(0, 0, 0, 0);
-  // Per-layer W1c.W_s table (16-bit) and the logit head (fp32) stay resident.
-  for (int e = tid; e < 3 * kV * kH; e += kThreadsB) {
-    const int l = e / (kV * kH), r = e % (kV * kH);
-    StabS[e] = to16<F16>(w.Stab[l][r]);
-  }
-  for (int e = tid; e < kH * kV; e += kThreadsB) {
-    const int v = e / kH, f = e % kH;
-    HeadS[v * kHeadPitch + f] = w.headT[f * kV + v];
-  }
   if (warp == 0) {
     tmem_alloc(&M.tbase, kTmemCols);
     tmem_relinquish();
@@ -400,7 +371,9 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       }
     };
     // GELU(A_t + W1b h_E + V + W1c W_s[tok]) into the SW128 operand of chunk c.
-    auto build_operand = [&](int c, const uint16_t* StabL,
+    // The table terms are widened and added in fp32 (W1c W_s[tok] from the
+    // fp32 table in global memory, an L1-resident 10.5 KiB per layer).
+    auto build_operand = [&](int c, const float* StabL,
                              const uint4 (&pe_raw)[kRowsPerThread],
                              const uint4 (&v_raw)[kRowsPerThread]) {
       unsigned char* dst = sm + kOffG1 + (c & 1) * kG1Bytes;
@@ -415,22 +388,16 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           const int code = Nb[s][k];
           const bool bw = (code >> 16) & 1;
           const int tok = code >> 17;
-          const uint4 stv =
-              bw ? reinterpret_cast<const uint4*>(StabL + tok * kH)[c8] : make_uint4(0, 0, 0, 0);
-          float tsum[8];
-          if constexpr (F16) {
-            // fp16: the three table terms add in half2 pairs (one unbiased
-            // rounding more than fp32 adds), then the fp32 node term
-            unpack8<F16>(add3_16<F16>(pe_raw[i], v_raw[i], stv), tsum);
-          } else {
-            // bf16's 8-bit mantissa is too coarse for that: fp32 adds
-            float pe[8], pv[8], st[8];
-            unpack8<F16>(pe_raw[i], pe);
-            unpack8<F16>(v_raw[i], pv);
-            unpack8<F16>(stv, st);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) tsum[q] = pe[q] + pv[q] + st[q];
+          float pe[8], pv[8];
+          unpack8<F16>(pe_raw[i], pe);
+          unpack8<F16>(v_raw[i], pv);
+          float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+          if (bw) {
+            const float4* st = reinterpret_cast<const float4*>(StabL + tok * kH) + c8 * 2;
+            s0 = __ldg(st);
+            s1 = __ldg(st + 1);
           }
+          const float st8[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
           const float4 a0 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2];
           const float4 a1 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2 + 1];
           const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
@@ -438,9 +405,12 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           // b2 (W2 is linear and a power-of-two scale is exact)
           float2 y[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            y[q] = gelu2_tc_x2(__fadd2_rn(make_float2(av[2 * q], av[2 * q + 1]),
-                                          make_float2(tsum[2 * q], tsum[2 * q + 1])));
+          for (int q = 0; q < 4; ++q) {
+            const float2 t2 = __fadd2_rn(__fadd2_rn(make_float2(pe[2 * q], pe[2 * q + 1]),
+                                                    make_float2(pv[2 * q], pv[2 * q + 1])),
+                                         make_float2(st8[2 * q], st8[2 * q + 1]));
+            y[q] = gelu2_tc_x2(__fadd2_rn(make_float2(av[2 * q], av[2 * q + 1]), t2));
+          }
           outv = make_uint4(pack16<F16>(y[0].x, y[0].y), pack16<F16>(y[1].x, y[1].y),
                             pack16<F16>(y[2].x, y[2].y), pack16<F16>(y[3].x, y[3].y));
         }
@@ -505,7 +475,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           bulk_prefetch_l2(tb.PE[l < 2 ? l + 1 : 0] + (int64_t)(M.off[gtid] + t) * kK * kH,
                            (uint32_t)(K * kH * 2));
         }
-        const uint16_t* StabL = StabS + l * kV * kH;
+        const float* StabL = w.Stab[l];
         const float2 half2c = make_float2(0.5f, 0.5f);
         const float b2 = w.b2[l][feat];
         const float2 b2p = make_float2(b2, b2);
@@ -654,13 +624,17 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       // ---- FFN: DO = sum_i W_out[:, i] GELU(W_in[i] h1 + b_in[i]) ----------
       for (int i = 0; i < 4; ++i) {
         if (tid == 0) {
-          const uint32_t wa = stream_wait(tile, sm, M, err);
+          uint32_t wa = stream_wait(tile, sm, M, err);
           tc_fence_after();
           if (!*abort_p)
             mma_k128(tm + kColDF, wa, smem_u32(sm + kOffH1b), kGB, idesc16<F16>(128, kGB), false);
+          wa = stream_wait(tile + 1, sm, M, err);
+          tc_fence_after();
+          if (!*abort_p)
+            mma_k128(tm + kColDF, wa, smem_u32(sm + kOffH1b), kGB, idesc16<F16>(128, kGB), true);
           mma_commit(&M.bar_all);
         }
-        ++tile;                                 // W_in[i]
+        tile += 2;                              // W_in[i] and its remainder
         if (!mbar_wait(&M.bar_all, ph_all, err)) *abort_p = 1;
         ph_all ^= 1;
         tc_fence_after();
@@ -754,7 +728,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       if (s < n) {
         z = w.head_b[v];
         const float4* hr = reinterpret_cast<const float4*>(hS[s]);
-        const float4* wr = reinterpret_cast<const float4*>(HeadS + v * kHeadPitch);
+        const float4* wr = reinterpret_cast<const float4*>(HeadS + v * kHeadPitch);   // L1
 #pragma unroll 8
         for (int f4 = 0; f4 < kH / 4; ++f4) {   // same fma order as f = 0..127
           const float4 h = hr[f4], wv = wr[f4];

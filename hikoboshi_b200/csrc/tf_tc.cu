@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_node_tc_kernel(const __grid_
   const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
   const int64_t tiles = (p.rows + 127) / 128;
   const bool last = p.layer == 2;
-  const int per_tile = last ? 9 : 11;
+  const int per_tile = last ? 13 : 15;
   const uint32_t idesc = idesc_h(128, 128);
 
   if (tid == 0) {
@@ -444,12 +444,15 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_node_tc_kernel(const __grid_
     __syncthreads();
     // ---- FFN: DO = sum_i W_out[:, i] GELU(W_in[i] h1 + b_in[i]) ------------
     if (tid == 0) {
-      const uint32_t w = ring_wait(j, sm, full, p.err, ok);
+      uint32_t w = ring_wait(j, sm, full, p.err, ok);       // W_in[0]
       tc_fence_after();
       if (ok) mma_k128(tm + kNColIn, smem_u32(Aop), w, 128, idesc, false);
+      w = ring_wait(j + 1, sm, full, p.err, ok);            // and its remainder
+      tc_fence_after();
+      if (ok) mma_k128(tm + kNColIn, smem_u32(Aop), w, 128, idesc, true);
       mma_commit(&bar_mma);
     }
-    ++j;
+    j += 2;
     mma_wait();
     for (int i = 0; i < 4; ++i) {
       unsigned char* F = sm + kNOffF + (i & 1) * kW128;
@@ -476,14 +479,17 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_node_tc_kernel(const __grid_
         tc_fence_after();
         if (ok) mma_k128(tm + kNColOut, smem_u32(F), w, 128, idesc, i > 0);
         if (i < 3) {
+          const uint32_t din = tm + kNColIn + (uint32_t)(((i + 1) & 1) * 128);
           w = ring_wait(j + 1, sm, full, p.err, ok);      // W_in[i + 1]
           tc_fence_after();
-          if (ok) mma_k128(tm + kNColIn + (uint32_t)(((i + 1) & 1) * 128), smem_u32(Aop), w, 128,
-                           idesc, false);
+          if (ok) mma_k128(din, smem_u32(Aop), w, 128, idesc, false);
+          w = ring_wait(j + 2, sm, full, p.err, ok);      // and its remainder
+          tc_fence_after();
+          if (ok) mma_k128(din, smem_u32(Aop), w, 128, idesc, true);
         }
         mma_commit(&bar_mma);
       }
-      j += i < 3 ? 2 : 1;
+      j += i < 3 ? 3 : 1;
       mma_wait();
     }
     if (tid == 0) {
