@@ -14,6 +14,8 @@
 
 #include <sched.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "host_order.hpp"
 #include "safetensors.hpp"
 
@@ -51,6 +53,17 @@ size_t Workspace::bytes() const {
 namespace {
 
 constexpr hkb_status kOk{HKB_OK, ""};
+
+// NVTX range over the host-side enqueue of one pipeline phase (featurise +
+// encode, decoder tables, decode / teacher-forced layers): profilers show it
+// on the CPU timeline and correlate it with the phase's kernels.  Costs
+// nothing unless a tool is attached.
+struct PhaseRange {
+  explicit PhaseRange(const char* name) { nvtxRangePushA(name); }
+  ~PhaseRange() { nvtxRangePop(); }
+  PhaseRange(const PhaseRange&) = delete;
+  PhaseRange& operator=(const PhaseRange&) = delete;
+};
 
 hkb_status invalid(const char* d) { return {HKB_INVALID_ARGUMENT, d}; }
 hkb_status internal(const char* d) { return {HKB_INTERNAL_ERROR, d}; }
@@ -1024,6 +1037,10 @@ hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   a.mask = eo.mask;
   a.e_idx = eo.e_idx;
   a.total_rows = hb.Q;
+  if (e->stall_check_calls > 0) {
+    a.stall_check = 1;
+    --e->stall_check_calls;
+  }
   launch_ar_decode_tc(st, db.bv, e->wbf, tb, a, f16, e->d_err);
   launch_scores(st, db.bv, o.tokens, o.log_probs, eo.mask, o.scores);
   e->launches += 2;
@@ -1193,24 +1210,32 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
   // fp32: SIMT parity pipeline; bf16: fp32 encoder, tables rounded to bf16;
   // f16: tensor-core encoder writing fp16 tables.
   const bool tc_encoder = e->precision == HKB_PRECISION_F16;
-  s = tc_encoder ? encode_tc(e, *hb, db, &eo) : encode_f32(e, *hb, db, &eo);
+  {
+    PhaseRange r("hkb.featurise+encode");
+    s = tc_encoder ? encode_tc(e, *hb, db, &eo) : encode_f32(e, *hb, db, &eo);
+  }
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[1], st));
   DecoderTables dt{};
   Bf16DecodeTables tb{};
-  if (tc_encoder) {
-    s = decoder_tables_tc(e, *hb, eo, &tb);
-  } else {
-    s = decoder_tables_f32(e, *hb, eo, &dt);
-    if (s.code == HKB_OK && e->precision == HKB_PRECISION_BF16)
-      s = decoder_tables_bf16(e, *hb, eo, dt, &tb);
+  {
+    PhaseRange r("hkb.decoder_tables");
+    if (tc_encoder) {
+      s = decoder_tables_tc(e, *hb, eo, &tb);
+    } else {
+      s = decoder_tables_f32(e, *hb, eo, &dt);
+      if (s.code == HKB_OK && e->precision == HKB_PRECISION_BF16)
+        s = decoder_tables_bf16(e, *hb, eo, dt, &tb);
+    }
+    if (s.code == HKB_OK) s = finish_orders(e, *hb, batch->decode_orders, out.orders);
   }
   if (s.code != HKB_OK) return s;
-  s = finish_orders(e, *hb, batch->decode_orders, out.orders);
-  if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[2], st));
-  s = e->precision == HKB_PRECISION_FP32 ? decode_f32(e, *hb, db, eo, dt, out)
-                                          : decode_tc(e, *hb, db, eo, tb, out);
+  {
+    PhaseRange r("hkb.decode");
+    s = e->precision == HKB_PRECISION_FP32 ? decode_f32(e, *hb, db, eo, dt, out)
+                                            : decode_tc(e, *hb, db, eo, tb, out);
+  }
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[3], st));
   HKB_CUDA(cudaGetLastError());
@@ -1268,10 +1293,14 @@ hkb_status score_tc(hkb_engine* e, const hkb_score_batch* batch, HostBatch& hb,
     if (s.code != HKB_OK) return s;
   }
   EncoderOut eo;
-  s = encode_tc(e, hb, db, &eo);
+  {
+    PhaseRange r("hkb.featurise+encode");
+    s = encode_tc(e, hb, db, &eo);
+  }
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaEventRecord(e->ev[1], st));
   Bf16DecodeTables tb{};
+  PhaseRange r_tab("hkb.decoder_tables+teacher_forced_layers");
   s = decoder_tables_tc(e, hb, eo, &tb, /*with_pe=*/false);
   if (s.code != HKB_OK) return s;
   if (!batch->orders) {
@@ -1421,6 +1450,9 @@ hkb_status hkb_mpnn_create(const void* st_blob, size_t length, int device,
   // Test hook: HKB_RECHECK_ALL_ORDERS=1 sends every random order through the
   // host recomputation path.
   if (const char* v = std::getenv("HKB_RECHECK_ALL_ORDERS")) e->recheck_all_orders = v[0] == '1';
+  // Test hook: the next HKB_STALL_CHECK_CALLS tensor-core design calls run the
+  // decode kernel's failure-path check (a bounded wait that runs out).
+  if (const char* v = std::getenv("HKB_STALL_CHECK_CALLS")) e->stall_check_calls = std::atoi(v);
   if (cudaMemcpy(e->d_weights, P.blob.data.data(), e->weights_bytes,
                  cudaMemcpyHostToDevice) != cudaSuccess) {
     cudaGetLastError();

@@ -102,5 +102,6 @@ struct hkb_engine {
   unsigned int* h_recheck = nullptr;
   cudaEvent_t ev_recheck = nullptr;
   int recheck_all_orders = 0;
+  int stall_check_calls = 0;   // test hook: decode calls that run the failure-path check
   int64_t orders_rechecked = 0;
 };

@@ -228,6 +228,7 @@ struct ArBf16Args {
   const float* mask;
   const int* e_idx;
   int64_t total_rows;
+  int stall_check = 0;       // failure-path check: wait on an unarmed barrier, then return
 };
 
 // Fused encoder-layer kernels (tensor-core modes; h_E fp16 [R*48,128]).

@@ -204,6 +204,21 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   const int L = bv.prot_len[b];
   const int K = L < kK ? L : kK;
 
+  // Failure-path check (a.stall_check): wait, with the normal bounded wait, on
+  // a barrier that nothing ever arrives on.  The wait gives up after about a
+  // second, records kErrTimeout and the CTA returns before it allocates tensor
+  // memory or issues any copy, so the caller sees InternalError and the context
+  // stays usable.
+  if (a.stall_check) {
+    if (tid == 0) {
+      mbar_init(&M.bar_all, 1);
+      fence_barrier_init();
+      mbar_wait(&M.bar_all, 0, err);
+    }
+    __syncthreads();
+    return;
+  }
+
   if (tid == 0) {
     for (int i = 0; i < kSlots; ++i) mbar_init(&M.full[i], 1);
     mbar_init(&M.bar_d2[0], 1);

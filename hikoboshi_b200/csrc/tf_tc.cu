@@ -49,17 +49,28 @@ __device__ __forceinline__ float h2f(uint16_t v) {
 // ---------------------------------------------------------------------------
 // Slot kernel
 // ---------------------------------------------------------------------------
-constexpr int kSubRows = 4;                        // rows per W2 MMA
+// Two ping-pong groups of 8 warps.  Per work item (one residue t) the CTA
+// forms D1 = W1b h_E[t] once; then group g takes the sub-tiles g, g+2, ... of
+// two sequences (96 slots) each: it stages the slots' gather addresses,
+// builds its G operand, issues its W2 MMA into its own TMEM columns and sums
+// the slots, so that one group's MMA wait and slot sum overlap the other
+// group's gathers and GELUs.  A thread owns one feature (f = TMEM lane) of one
+// row of its group's sub-tile.
+constexpr int kSubRows = 2;                        // rows per W2 MMA and group
+constexpr int kSubN = kSubRows * kK;               // 96 slots
 constexpr uint32_t kSOffW1b = 0;
 constexpr uint32_t kSOffW2 = kW128;
 constexpr uint32_t kSOffE = 2 * kW128;             // 2 h_E tiles of 48 rows
 constexpr uint32_t kETileBytes = kK * 256;         // 12 KiB
 constexpr uint32_t kSOffG = kSOffE + 2 * kETileBytes;
-constexpr uint32_t kGBytes = kSubRows * kK * 256;  // 48 KiB
-constexpr uint32_t kSOffStab = kSOffG + kGBytes;   // fp32 [21,128]
-constexpr uint32_t kSOffCode = kSOffStab + kV * kH * 4;   // int [4][48]
-constexpr uint32_t kSOffJ = kSOffCode + kSubRows * kK * 4; // int [48] local neighbour
+constexpr uint32_t kGBytes = kSubN * 256;          // 24 KiB per group
+constexpr uint32_t kSOffStab = kSOffG + 2 * kGBytes;   // fp32 [21,128]
+constexpr uint32_t kSOffSrc = kSOffStab + kV * kH * 4; // per group, 2 buffers: [96] gather offsets
+constexpr uint32_t kSOffSt = kSOffSrc + 4 * kSubN * 8; // per group, 2 buffers: [96] Stab row
+constexpr uint32_t kSOffJ = kSOffSt + 4 * kSubN * 4;   // int [48] local neighbour
 constexpr uint32_t kSlotSmem = kSOffJ + kK * 4 + 1024;
+constexpr uint32_t kTfColD2 = 64;                  // group g: columns 64 + 96 g
+constexpr int kGroupThreadsTf = 256;
 
 __device__ __forceinline__ void load_etile(unsigned char* tile, const uint16_t* h_e, int64_t row0,
                                            int64_t row_end, int tid) {
@@ -75,22 +86,29 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float* StabS = reinterpret_cast<float*>(sm + kSOffStab);
-  int (*code)[kK] = reinterpret_cast<int (*)[kK]>(sm + kSOffCode);
   int* SJ = reinterpret_cast<int*>(sm + kSOffJ);
-  __shared__ uint64_t bar_w, bar_mma;
+  __shared__ uint64_t bar_w, bar_d1, bar_d2[2];
   __shared__ uint32_t tmem_base;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quad = warp & 3, rho = warp >> 2;   // feature quadrant, row of the sub-tile
+  const int grp = warp >> 3, gtid = tid & (kGroupThreadsTf - 1);
+  const int quad = warp & 3, rho = (warp >> 2) & 1;   // feature quadrant, row of the sub-tile
   const int f = quad * 32 + lane;
   const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
   const int R = p.bv.total_residues;
   const int64_t SL = (int64_t)R * kK;
   const int l = p.layer;
+  int64_t* SRC0 = reinterpret_cast<int64_t*>(sm + kSOffSrc) + grp * 2 * kSubN;   // element offsets
+  int* STR0 = reinterpret_cast<int*>(sm + kSOffSt) + grp * 2 * kSubN;
+  unsigned char* G = sm + kSOffG + grp * kGBytes;
+  // gather source of a slot: PV (bit 62 set) or PVenc rows, as element offsets
+  const uint16_t* PVl = l == 0 ? p.PVenc : p.PV;
 
   if (tid == 0) {
     mbar_init(&bar_w, 1);
-    mbar_init(&bar_mma, 1);
+    mbar_init(&bar_d1, 1);
+    mbar_init(&bar_d2[0], 1);
+    mbar_init(&bar_d2[1], 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -110,7 +128,7 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
     }
   }
   bool ok = mbar_wait(&bar_w, 0, p.err);
-  uint32_t ph = 0;
+  uint32_t ph1 = 0, ph2 = 0;
   const float b2 = p.b2[f];
   const float2 b2p = make_float2(b2, b2);
   const float2 halfc = make_float2(0.5f, 0.5f);
@@ -120,8 +138,7 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
   cp_async_commit();
   for (int it = 0; r < R; r += gridDim.x, ++it) {
     if (__syncthreads_or(!ok)) break;
-    const int buf = it & 1;
-    unsigned char* etile = sm + kSOffE + buf * kETileBytes;
+    unsigned char* etile = sm + kSOffE + (it & 1) * kETileBytes;
     const int b = p.bv.res_prot[r];
     const int L = p.bv.prot_len[b];
     const int K = L < kK ? L : kK;
@@ -135,13 +152,8 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
     if (tid == 0) {
       tc_fence_after();
       mma_k128(tm, smem_u32(sm + kSOffW1b), smem_u32(etile), kK, idesc_h(128, kK), false);
-      mma_commit(&bar_mma);
+      mma_commit(&bar_d1);
     }
-    // the next residue's h_E rows into the other buffer (last read by the
-    // previous item's D1 MMA, which completed before its epilogue)
-    const int rn = r + gridDim.x;
-    if (rn < R) load_etile(sm + kSOffE + (buf ^ 1) * kETileBytes, p.h_e, (int64_t)rn * kK, SL, tid);
-    cp_async_commit();
     if (tid < kK) {
       int j = -1;
       if (tid < K) {
@@ -153,81 +165,106 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
       }
       SJ[tid] = j;
     }
-    if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
-    ph ^= 1;
+    if (!mbar_wait(&bar_d1, ph1, p.err)) ok = false;
+    ph1 ^= 1;
     tc_fence_after();
+    // the other h_E buffer was last read by the previous item's D1 MMA
+    const int rn = r + gridDim.x;
+    if (rn < R) load_etile(sm + kSOffE + ((it + 1) & 1) * kETileBytes, p.h_e, (int64_t)rn * kK, SL, tid);
+    cp_async_commit();
     float d1[kK];
     tmem_ld48(tm + lane_base, d1);
-    __syncthreads();   // SJ visible
-    for (int s0 = 0; s0 < nseq; s0 += kSubRows) {
+    tc_fence_before();
+    __syncthreads();   // SJ visible; D1 read by every thread before the next item's MMA
+    // Gather addresses of sub-tile `sub` into address buffer `ab` (threads
+    // gtid < 96 of the group; their global loads overlap the group's MMA).
+    auto stage = [&](int sub, int ab) {
+      if (gtid < kSubN && sub * kSubRows < nseq) {
+        const int s0 = sub * kSubRows;
+        const int nrows = nseq - s0 < kSubRows ? nseq - s0 : kSubRows;
+        const int rr = gtid / kK, k = gtid % kK;
+        int64_t src = -1;
+        int st = -1;
+        const int j = SJ[k];
+        if (rr < nrows && j >= 0) {
+          const int64_t qs = p.bv.seq_row_off[seq0 + s0 + rr];
+          const int64_t qj = qs + j;
+          if (p.pos[qj] < p.pos[qs + t]) {   // decoded neighbour: its own row
+            src = (l == 0 ? (int64_t)(off + j) : qj) * kH;
+            st = p.tokens[qj] * kH;
+          } else {                           // undecoded: the encoder row
+            src = ((int64_t)(off + j) * kH) | (1ll << 62);
+          }
+        }
+        SRC0[ab * kSubN + gtid] = src;
+        STR0[ab * kSubN + gtid] = st;
+      }
+    };
+    stage(grp, 0);
+    named_bar_sync(1 + grp, kGroupThreadsTf);
+    int ab = 0;
+    for (int sub = grp; sub * kSubRows < nseq; sub += 2, ab ^= 1) {
+      const int s0 = sub * kSubRows;
       const int nrows = nseq - s0 < kSubRows ? nseq - s0 : kSubRows;
       const int N = nrows * kK;
-      // slot codes: j | bw << 16 | tok << 17 (-1 for an empty slot)
-      if (tid < nrows * kK) {
-        const int rr = tid / kK, k = tid % kK;
-        const int64_t qs = p.bv.seq_row_off[seq0 + s0 + rr];
-        const int j = SJ[k];
-        int c = -1;
-        if (j >= 0) {
-          const int64_t qj = qs + j;
-          const bool bw = p.pos[qj] < p.pos[qs + t];
-          const int tok = p.tokens[qj];
-          c = j | (bw ? 1 << 16 : 0) | (tok << 17);
-        }
-        code[rr][k] = c;
-      }
-      __syncthreads();
-      unsigned char* G = sm + kSOffG;
+      const int64_t* SRC = SRC0 + ab * kSubN;
+      const int* STR = STR0 + ab * kSubN;
       int64_t q = -1;
       if (rho < nrows) {
         const int64_t qs = p.bv.seq_row_off[seq0 + s0 + rho];
         q = qs + t;
         const float a = l == 0 ? p.Aenc0[(int64_t)r * kH + f] : p.A[q * kH + f];
 #pragma unroll
-        for (int k = 0; k < kK; k += 2) {
-          float x[2];
+        for (int h = 0; h < 2; ++h) {
+          // 24 slots: all gathers first, then the GELUs
+          uint16_t raw[24];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int c = code[rho][k + u];
-            float v = 0.0f;
-            if (c >= 0) {
-              const int j = c & 0xFFFF;
-              if ((c >> 16) & 1) {
-                const float pv = l == 0 ? h2f(p.PVenc[(int64_t)(off + j) * kH + f])
-                                        : h2f(p.PV[(qs + j) * kH + f]);
-                v = pv + StabS[(c >> 17) * kH + f];
-              } else {
-                v = h2f(p.PVenc[(int64_t)(off + j) * kH + f]);
-              }
+          for (int u = 0; u < 24; ++u) {
+            const int64_t src = SRC[rho * kK + h * 24 + u];
+            raw[u] = 0;
+            if (src >= 0) {
+              const uint16_t* base = (src >> 62) ? p.PVenc : PVl;
+              raw[u] = base[(src & ~(1ll << 62)) + f];
             }
-            x[u] = d1[k + u] + a + v;
           }
-          // the operand holds 2 GELU(x); the epilogue halves D2 (exact)
-          const float2 y = gelu2_tc_x2(make_float2(x[0], x[1]));
-          const int c0 = code[rho][k], c1 = code[rho][k + 1];
-          *reinterpret_cast<__half*>(G + sw128_offset(rho * kK + k, f, N)) =
-              __float2half_rn(c0 >= 0 ? y.x : 0.0f);
-          *reinterpret_cast<__half*>(G + sw128_offset(rho * kK + k + 1, f, N)) =
-              __float2half_rn(c1 >= 0 ? y.y : 0.0f);
+#pragma unroll
+          for (int u = 0; u < 24; u += 2) {
+            float x[2];
+#pragma unroll
+            for (int w = 0; w < 2; ++w) {
+              const int st = STR[rho * kK + h * 24 + u + w];
+              x[w] = d1[h * 24 + u + w] + a + h2f(raw[u + w]) + (st >= 0 ? StabS[st + f] : 0.0f);
+            }
+            // the operand holds 2 GELU(x); the epilogue halves D2 (exact)
+            const float2 y = gelu2_tc_x2(make_float2(x[0], x[1]));
+            const int k = h * 24 + u;
+            const bool v0 = SRC[rho * kK + k] >= 0, v1 = SRC[rho * kK + k + 1] >= 0;
+            *reinterpret_cast<__half*>(G + sw128_offset(rho * kK + k, f, N)) =
+                __float2half_rn(v0 ? y.x : 0.0f);
+            *reinterpret_cast<__half*>(G + sw128_offset(rho * kK + k + 1, f, N)) =
+                __float2half_rn(v1 ? y.y : 0.0f);
+          }
         }
       }
       fence_async_smem();
       tc_fence_before();
-      __syncthreads();
-      if (tid == 0) {
+      named_bar_sync(1 + grp, kGroupThreadsTf);
+      if (gtid == 0) {
         tc_fence_after();
-        if (ok) mma_k128(tm + 64, smem_u32(sm + kSOffW2), smem_u32(G), N, idesc_h(128, N), false);
-        mma_commit(&bar_mma);
+        if (ok) mma_k128(tm + kTfColD2 + grp * kSubN, smem_u32(sm + kSOffW2), smem_u32(G), N,
+                         idesc_h(128, N), false);
+        mma_commit(&bar_d2[grp]);
       }
-      if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
-      ph ^= 1;
+      stage(sub + 2, ab ^ 1);   // the next sub-tile's addresses while the MMA runs
+      if (!mbar_wait(&bar_d2[grp], ph2, p.err)) ok = false;
+      ph2 ^= 1;
       tc_fence_after();
       if (rho < nrows) {
         float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
 #pragma unroll
         for (int k0 = 0; k0 < kK; k0 += 16) {
           float v[16];
-          tmem_ld16(tm + lane_base + 64u + (uint32_t)(rho * kK + k0), v);
+          tmem_ld16(tm + lane_base + kTfColD2 + (uint32_t)(grp * kSubN + rho * kK + k0), v);
 #pragma unroll
           for (int k = 0; k < 16; k += 2) {
             float2 g = gelu2_tc_x2(__ffma2_rn(make_float2(v[k], v[k + 1]), halfc, b2p));
@@ -239,7 +276,7 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
         p.S[q * kH + f] = 0.5f * ((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y));
       }
       tc_fence_before();
-      __syncthreads();   // G and the codes are rewritten by the next sub-tile
+      named_bar_sync(1 + grp, kGroupThreadsTf);   // G free, next addresses staged
     }
   }
   cp_async_wait_all();

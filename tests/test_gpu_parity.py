@@ -217,3 +217,29 @@ def test_device_orders_match_host_orders(weights_path):
         assert (res2.orders[b] == res.orders[b]).all()
         assert (res2.tokens[b] == res.tokens[b]).all()
         assert (res2.log_probs[b] == res.log_probs[b]).all()
+
+
+def test_decode_wait_timeout_returns_internal_error(weights_path):
+    """The failure path of the bounded waits: the decode kernel's check mode
+    waits on a barrier nothing arrives on; after about a second the wait gives
+    up, the kernel records the timeout and returns, and the call reports
+    InternalError with the timeout detail.  The next call on the same engine
+    succeeds (nothing faulted, the context is intact)."""
+    import os
+    from hikoboshi_b200 import DesignEngine, HkbError, synthetic_backbone
+    c, s = synthetic_backbone(5, 64)
+    os.environ["HKB_STALL_CHECK_CALLS"] = "1"
+    try:
+        eng = DesignEngine(weights_path, device=0, precision="f16")
+    finally:
+        del os.environ["HKB_STALL_CHECK_CALLS"]
+    try:
+        with pytest.raises(HkbError) as e:
+            eng.design([c], [s], num_seqs=2, seeds=1, temperatures=0.1)
+        assert e.value.code == 5 and "timed out" in e.value.detail, e.value.detail
+        res = eng.design([c], [s], num_seqs=2, seeds=1, temperatures=0.1)
+        assert ((res.tokens[0] >= 0) & (res.tokens[0] < 21)).all()
+        lse = np.log(np.exp(res.log_probs[0].astype(np.float64)).sum(-1))
+        assert np.abs(lse).max() < 1e-4
+    finally:
+        eng.close()
