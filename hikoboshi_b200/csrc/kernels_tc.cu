@@ -51,6 +51,7 @@ constexpr uint32_t kColA = 192;
 constexpr uint32_t kColPV = 208;
 constexpr uint32_t kColD3 = 224;
 constexpr uint32_t kColDF = 240;
+constexpr uint32_t kColDF2 = 272;  // W_in remainder product (issued by a second thread)
 constexpr uint32_t kColDO = 256;
 constexpr uint32_t kTmemCols = 512;
 
@@ -79,6 +80,7 @@ struct Misc {
   uint64_t full[kSlots];
   uint64_t bar_d2[2];     // message MMA of group g's chunk complete (D2 buffer g full)
   uint64_t bar_all;
+  uint64_t bar_two;       // two issuing threads' MMAs complete (node terms, W_in hi / remainder)
   uint32_t tbase;
   int abort_flag;
   int t[kGB];
@@ -224,6 +226,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     mbar_init(&M.bar_d2[0], 1);
     mbar_init(&M.bar_d2[1], 1);
     mbar_init(&M.bar_all, 1);
+    mbar_init(&M.bar_two, 2);
     M.abort_flag = 0;
     fence_barrier_init();
   }
@@ -270,7 +273,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   volatile int* abort_p = &M.abort_flag;
   uint4 raw_pe[kRowsPerThread], raw_v[kRowsPerThread];   // in-flight slot rows
   uint32_t d2_count = 0;   // this group's message MMAs waited for so far
-  uint32_t ph_all = 0;
+  uint32_t ph_all = 0, ph_two = 0;
   int tile = 0;   // next tile to consume (same on all threads)
 
   // The next position's h_enc / Aenc0 rows (residue t_next of each sequence)
@@ -439,8 +442,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       // ---- node terms for l >= 1 (MMAs issued at the end of layer l-1) -----
       if (l > 0) {
         const float b1 = w.b1[l][feat];        // in flight during the wait
-        if (!mbar_wait(&M.bar_all, ph_all, err)) *abort_p = 1;
-        ph_all ^= 1;
+        if (!mbar_wait(&M.bar_two, ph_two, err)) *abort_p = 1;
+        ph_two ^= 1;
         tc_fence_after();
         if (tid == 0) {
           st.used = tile;                       // W1a, W1d of this layer released
@@ -638,28 +641,32 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       }
       // ---- FFN: DO = sum_i W_out[:, i] GELU(W_in[i] h1 + b_in[i]) ----------
       for (int i = 0; i < 4; ++i) {
-        if (tid == 0) {
-          uint32_t wa = stream_wait(tile, sm, M, err);
+        // W_in[i] by thread 0 and its remainder by thread 32, into separate
+        // accumulators (summed in the epilogue): the two MMA streams issue
+        // side by side
+        if (tid == 0 || tid == 32) {
+          const int j = tid == 0 ? tile : tile + 1;
+          const uint32_t wa = stream_wait(j, sm, M, err);
           tc_fence_after();
           if (!*abort_p)
-            mma_k128(tm + kColDF, wa, smem_u32(sm + kOffH1b), kGB, idesc16<F16>(128, kGB), false);
-          wa = stream_wait(tile + 1, sm, M, err);
-          tc_fence_after();
-          if (!*abort_p)
-            mma_k128(tm + kColDF, wa, smem_u32(sm + kOffH1b), kGB, idesc16<F16>(128, kGB), true);
-          mma_commit(&M.bar_all);
+            mma_k128(tm + (tid == 0 ? kColDF : kColDF2), wa, smem_u32(sm + kOffH1b), kGB,
+                     idesc16<F16>(128, kGB), false);
+          mma_commit(&M.bar_two);
         }
         tile += 2;                              // W_in[i] and its remainder
-        if (!mbar_wait(&M.bar_all, ph_all, err)) *abort_p = 1;
-        ph_all ^= 1;
+        if (!mbar_wait(&M.bar_two, ph_two, err)) *abort_p = 1;
+        ph_two ^= 1;
         tc_fence_after();
         if (tid == 0) {
           st.used = tile;
           stream_issue(st, sm, M, w.stream);
         }
         {
-          float v[4];
+          float v[4], v2[4];
           tmem_ld4(tm + lane_base + kColDF + wg * 4, v);
+          tmem_ld4(tm + lane_base + kColDF2 + wg * 4, v2);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v[q] += v2[q];
           const float bi = i == 0 ? b_in0 : i == 1 ? b_in1 : i == 2 ? b_in2 : b_in3;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -718,16 +725,13 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       __syncthreads();
       // ---- next layer's node terms: W1a h, W1d h ------------------------------
       if (l < 2) {
-        if (tid == 0) {
-          uint32_t wa = stream_wait(tile, sm, M, err);
+        if (tid == 0 || tid == 32) {   // W1a by thread 0, W1d by thread 32
+          const uint32_t wa = stream_wait(tid == 0 ? tile : tile + 1, sm, M, err);
           tc_fence_after();
           if (!*abort_p)
-            mma_k128(tm + kColA, wa, smem_u32(sm + kOffHb), kGB, idesc16<F16>(128, kGB), false);
-          wa = stream_wait(tile + 1, sm, M, err);
-          tc_fence_after();
-          if (!*abort_p)
-            mma_k128(tm + kColPV, wa, smem_u32(sm + kOffHb), kGB, idesc16<F16>(128, kGB), false);
-          mma_commit(&M.bar_all);
+            mma_k128(tm + (tid == 0 ? kColA : kColPV), wa, smem_u32(sm + kOffHb), kGB,
+                     idesc16<F16>(128, kGB), false);
+          mma_commit(&M.bar_two);
         }
         tile += 2;                              // W1a, W1d of layer l+1 (released
                                                 // after the wait at its start)
