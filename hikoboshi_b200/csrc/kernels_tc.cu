@@ -80,7 +80,8 @@ struct Misc {
   uint64_t full[kSlots];
   uint64_t bar_d2[2];     // message MMA of group g's chunk complete (D2 buffer g full)
   uint64_t bar_all;
-  uint64_t bar_two;       // two issuing threads' MMAs complete (node terms, W_in hi / remainder)
+  uint64_t bar_two;       // two issuing threads' MMAs complete (node terms)
+  uint64_t bar_ffn;       // three issuing threads' FFN MMAs complete
   uint32_t tbase;
   int abort_flag;
   int t[kGB];
@@ -227,6 +228,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     mbar_init(&M.bar_d2[1], 1);
     mbar_init(&M.bar_all, 1);
     mbar_init(&M.bar_two, 2);
+    mbar_init(&M.bar_ffn, 3);
     M.abort_flag = 0;
     fence_barrier_init();
   }
@@ -273,7 +275,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   volatile int* abort_p = &M.abort_flag;
   uint4 raw_pe[kRowsPerThread], raw_v[kRowsPerThread];   // in-flight slot rows
   uint32_t d2_count = 0;   // this group's message MMAs waited for so far
-  uint32_t ph_all = 0, ph_two = 0;
+  uint32_t ph_all = 0, ph_two = 0, ph_ffn = 0;
   int tile = 0;   // next tile to consume (same on all threads)
 
   // The next position's h_enc / Aenc0 rows (residue t_next of each sequence)
@@ -640,25 +642,29 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         }
       }
       // ---- FFN: DO = sum_i W_out[:, i] GELU(W_in[i] h1 + b_in[i]) ----------
-      for (int i = 0; i < 4; ++i) {
-        // W_in[i] by thread 0 and its remainder by thread 32, into separate
-        // accumulators (summed in the epilogue): the two MMA streams issue
-        // side by side
-        if (tid == 0 || tid == 32) {
-          const int j = tid == 0 ? tile : tile + 1;
-          const uint32_t wa = stream_wait(j, sm, M, err);
+      // Three issuing threads: thread 0 W_in[i] (into DF), thread 32 its
+      // remainder (into DF2, summed in the epilogue), thread 64 W_out[:, i]
+      // (the only writer of DO, so its accumulation stays ordered).  After
+      // GELU(i) the three issue W_out[:, i], W_in[i+1] and its remainder side
+      // by side; each commits to bar_ffn (three arrivals per phase), so one
+      // wait covers W_in[i+1] and W_out[:, i], which frees Fb for GELU(i+1).
+      if (tid == 0 || tid == 32 || tid == 64) {
+        if (tid != 64) {
+          const uint32_t wa = stream_wait(tid == 0 ? tile : tile + 1, sm, M, err);
           tc_fence_after();
           if (!*abort_p)
             mma_k128(tm + (tid == 0 ? kColDF : kColDF2), wa, smem_u32(sm + kOffH1b), kGB,
                      idesc16<F16>(128, kGB), false);
-          mma_commit(&M.bar_two);
         }
-        tile += 2;                              // W_in[i] and its remainder
-        if (!mbar_wait(&M.bar_two, ph_two, err)) *abort_p = 1;
-        ph_two ^= 1;
+        mma_commit(&M.bar_ffn);
+      }
+      tile += 2;                                // W_in[0] and its remainder
+      for (int i = 0; i < 4; ++i) {
+        if (!mbar_wait(&M.bar_ffn, ph_ffn, err)) *abort_p = 1;
+        ph_ffn ^= 1;
         tc_fence_after();
         if (tid == 0) {
-          st.used = tile;
+          st.used = tile;                       // every tile before W_out[:, i] is consumed
           stream_issue(st, sm, M, w.stream);
         }
         {
@@ -678,17 +684,25 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
-        if (tid == 0) {
-          const uint32_t wa = stream_wait(tile, sm, M, err);
-          tc_fence_after();
-          if (!*abort_p)
-            mma_k128(tm + kColDO, wa, smem_u32(sm + kOffFb), kGB, idesc16<F16>(128, kGB), i > 0);
+        if (tid == 0 || tid == 32 || tid == 64) {
+          if (tid == 64) {
+            const uint32_t wa = stream_wait(tile, sm, M, err);          // W_out[:, i]
+            tc_fence_after();
+            if (!*abort_p)
+              mma_k128(tm + kColDO, wa, smem_u32(sm + kOffFb), kGB, idesc16<F16>(128, kGB), i > 0);
+          } else if (i < 3) {
+            const uint32_t wa = stream_wait(tid == 0 ? tile + 1 : tile + 2, sm, M, err);
+            tc_fence_after();
+            if (!*abort_p)
+              mma_k128(tm + (tid == 0 ? kColDF : kColDF2), wa, smem_u32(sm + kOffH1b), kGB,
+                       idesc16<F16>(128, kGB), false);
+          }
+          mma_commit(&M.bar_ffn);
         }
-        ++tile;                                 // W_out[:, i]
+        tile += i < 3 ? 3 : 1;                  // W_out[:, i] (and W_in[i+1], remainder)
       }
-      if (tid == 0) mma_commit(&M.bar_all);
-      if (!mbar_wait(&M.bar_all, ph_all, err)) *abort_p = 1;
-      ph_all ^= 1;
+      if (!mbar_wait(&M.bar_ffn, ph_ffn, err)) *abort_p = 1;
+      ph_ffn ^= 1;
       tc_fence_after();
       if (tid == 0) {
         st.used = tile;
