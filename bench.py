@@ -781,16 +781,23 @@ def run_config5(args):
 
 
 def run_profile_case(args):
-    """One untimed design on a smaller case (64 backbones x L=128 x 32
-    sequences, T=0.1) for ncu captures: the same kernels as the bench step
-    with about half the device footprint."""
+    """One untimed call on a small case for ncu captures: ``design`` runs
+    N backbones x L=256 x 32 sequences (T=0.1), ``score`` the teacher-forced
+    pass over N backbones x L=384 x 16 random sequences (the config-2 and
+    config-4 shapes with N proteins, default 16)."""
     from hikoboshi_b200 import DesignEngine, synthetic_backbone
-    bb = [synthetic_backbone(i, 128) for i in range(N_PROT)]
+    n = args.profile_proteins
     eng = DesignEngine(WEIGHTS, device=0, precision=args.precision)
-    eng.design([b[0] for b in bb], [b[1] for b in bb], num_seqs=N_SEQ, seeds=list(range(N_PROT)),
-               temperatures=TEMP, keep_log_probs=True)
-    print(json.dumps({"profile_case": "64 x L=128 x 32", "precision": args.precision,
-                      **eng.last_timings()}))
+    if args.profile_workload == "score":
+        cs, ss, toks = config4_inputs(0, synthetic_backbone)
+        eng.score(cs[:n], ss[:n], toks[:n], seeds=3)
+        case = f"{n} x L=384 x 16 teacher-forced"
+    else:
+        bb = [synthetic_backbone(i, L_RES) for i in range(n)]
+        eng.design([b[0] for b in bb], [b[1] for b in bb], num_seqs=N_SEQ, seeds=list(range(n)),
+                   temperatures=TEMP, keep_log_probs=True)
+        case = f"{n} x L=256 x 32 design"
+    print(json.dumps({"profile_case": case, "precision": args.precision, **eng.last_timings()}))
     eng.close()
     return 0
 
@@ -807,7 +814,9 @@ def main():
                     help="config2 (default): batched design; config4: teacher-forced scoring; "
                          "config5: the mixed-length sweep sharded over the ranks")
     ap.add_argument("--profile-case", action="store_true",
-                    help="one untimed design on 64 x L=128 x 32 (for ncu captures)")
+                    help="one untimed call on a small case (for ncu captures)")
+    ap.add_argument("--profile-workload", choices=["design", "score"], default="design")
+    ap.add_argument("--profile-proteins", type=int, default=16)
     args = ap.parse_args()
     if args.profile_case:
         return run_profile_case(args)
