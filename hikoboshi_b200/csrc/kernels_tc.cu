@@ -12,13 +12,17 @@
 //   messages     D2  = W2 GELU(A_t + W1b h_E + ...)   M=128 N=96  K=128 (x8 chunks)
 //   aggregation  D3  = W3 (sum_k GELU(D2 + b2))       M=128 N=16  K=128
 //   FFN          DF  = W_in[i] h1,  DO += W_out[:, i] GELU(DF + b_in)  (i = 0..3)
-// The slot sum runs along a thread's own TMEM row, LayerNorm statistics are
-// warp reductions over a transposed fp32 copy, and the sampler is the
-// reference's (serial over 21 logits, double CDF).
+// W_in is applied as its fp16 value plus its fp16 remainder W_in - fp16(W_in)
+// (two products summed in fp32: about twice the 16-bit precision for the
+// decoder's most error-sensitive weight).  The slot sum runs along a thread's
+// own TMEM row, LayerNorm statistics are warp reductions over a transposed
+// fp32 copy, and the sampler is the reference's (serial over 21 logits,
+// double CDF).
 //
-// Weight tiles stream through a 3-slot shared-memory ring by 1-D bulk copies
-// (no tensor map) issued by thread 0 in consumption order.  The CTA has 16
-// warps.  In the message (slot) phase they form two ping-pong groups of 8
+// Weight tiles stream through a 4-slot shared-memory ring by 1-D bulk copies
+// (no tensor map) issued by thread 0 in consumption order; independent MMAs
+// of the node and FFN phases are issued by up to three threads.  The CTA has
+// 16 warps.  In the message (slot) phase they form two ping-pong groups of 8
 // warps; each group gathers the neighbour rows of its next chunk (in
 // registers, one chunk ahead), builds the GELU operand, issues the MMA and
 // sums GELU(D2 + b2) over the slots of its own chunks, so that one group's

@@ -9,14 +9,15 @@
 //     G  = GELU(D1 + A_row + V_slot)        per row (sequence) and slot k
 //        V_slot = PV_l[s, j] + W1c W_s[tok_j]   if pos_s(j) < pos_s(t)
 //               = W1d h_enc[j]                  otherwise
-//     D2 = W2 G                             N = 48 slots x up to 4 rows
+//     D2 = W2 G                             N = 48 slots x up to 2 rows
 //     S_row = sum_{k < K} GELU(D2 + b2)
 //   The W1b h_E term is computed once per residue and shared by its rows.
 //
 //   tf_node_tc   128 rows per tile (rows on TMEM lanes, weights as B)
 //     h1 = LN1(h + (W3 S + K b3) / 30)
 //     h' = LN2(h1 + W_out GELU(W_in h1 + b_in) + b_out) * m_t
-//     then the next layer's node terms A = W1a h' + b1 (fp32) and
+//     (W_in as fp16 value + fp16 remainder), then the next layer's node
+//     terms A = W1a h' + b1 (fp32) and
 //     PV = W1d h' (fp16), or, after the last layer, the logits and their
 //     unscaled log-softmax (log_softmax_scalar.cpp:8-37).
 //   Weight tiles stream through a 3-slot shared-memory ring by bulk copies.
