@@ -478,6 +478,20 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       mma_k128(tm, smem_u32(G), r, 128, idesc, true);
       mma_commit(&bar_mma);
     }
+    // the residual h_E row as its fp16 value plus fp16 remainder (the tile
+    // buffer already holds the next tile's rows; this row sits in L2), loaded
+    // while the W13 MMAs run
+    uint4 hres[4], lres[4];
+    {
+      const int64_t srow = (s < SL ? s : 0) * kH + c0;
+      const uint4* hrow = reinterpret_cast<const uint4*>(p.h_e + srow);
+      const uint4* lrow = reinterpret_cast<const uint4*>(p.h_e_lo + srow);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        hres[u] = hrow[u];
+        lres[u] = lrow[u];
+      }
+    }
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
@@ -487,14 +501,9 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     {
       float x[32];
       tmem_ld32(tm + lane_base + (uint32_t)c0, x);
-      // the residual h_E row as its fp16 value plus fp16 remainder (the tile
-      // buffer already holds the next tile's rows; this row sits in L2)
-      const int64_t srow = (s < SL ? s : 0) * kH + c0;
-      const uint4* hrow = reinterpret_cast<const uint4*>(p.h_e + srow);
-      const uint4* lrow = reinterpret_cast<const uint4*>(p.h_e_lo + srow);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const uint4 hv = hrow[u], lv = lrow[u];
+        const uint4 hv = hres[u], lv = lres[u];
         const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w}, lw[4] = {lv.x, lv.y, lv.z, lv.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {

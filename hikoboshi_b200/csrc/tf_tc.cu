@@ -65,13 +65,16 @@ constexpr uint32_t kSOffE = 2 * kW128;             // 2 h_E tiles of 48 rows
 constexpr uint32_t kETileBytes = kK * 256;         // 12 KiB
 constexpr uint32_t kSOffG = kSOffE + 2 * kETileBytes;
 constexpr uint32_t kGBytes = kSubN * 256;          // 24 KiB per group
-constexpr uint32_t kSOffStab = kSOffG + 2 * kGBytes;   // fp32 [21,128]
-constexpr uint32_t kSOffSrc = kSOffStab + kV * kH * 4; // per group, 2 buffers: [96] gather offsets
+constexpr uint32_t kSOffStab = kSOffG + 2 * kGBytes;   // fp32 [22,128] (row 21 zero)
+constexpr uint32_t kSOffSrc = kSOffStab + (kV + 1) * kH * 4; // per group, 2 buffers: [96] row pointers
 constexpr uint32_t kSOffSt = kSOffSrc + 4 * kSubN * 8; // per group, 2 buffers: [96] Stab row
 constexpr uint32_t kSOffJ = kSOffSt + 4 * kSubN * 4;   // int [48] local neighbour
 constexpr uint32_t kSlotSmem = kSOffJ + kK * 4 + 1024;
 constexpr uint32_t kTfColD2 = 64;                  // group g: columns 64 + 96 g
 constexpr int kGroupThreadsTf = 256;
+
+// The V row of a slot past K (its products are dropped by the slot sum).
+__device__ const uint16_t g_zero_row[kH] = {};
 
 __device__ __forceinline__ void load_etile(unsigned char* tile, const uint16_t* h_e, int64_t row0,
                                            int64_t row_end, int tid) {
@@ -99,11 +102,10 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
   const int R = p.bv.total_residues;
   const int64_t SL = (int64_t)R * kK;
   const int l = p.layer;
-  int64_t* SRC0 = reinterpret_cast<int64_t*>(sm + kSOffSrc) + grp * 2 * kSubN;   // element offsets
+  const uint16_t** SRC0 = reinterpret_cast<const uint16_t**>(sm + kSOffSrc) + grp * 2 * kSubN;
   int* STR0 = reinterpret_cast<int*>(sm + kSOffSt) + grp * 2 * kSubN;
   unsigned char* G = sm + kSOffG + grp * kGBytes;
-  // gather source of a slot: PV (bit 62 set) or PVenc rows, as element offsets
-  const uint16_t* PVl = l == 0 ? p.PVenc : p.PV;
+  const uint16_t* PVl = l == 0 ? p.PVenc : p.PV;   // decoded neighbours' rows
 
   if (tid == 0) {
     mbar_init(&bar_w, 1);
@@ -116,7 +118,7 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
     tmem_alloc(&tmem_base, 256);
     tmem_relinquish();
   }
-  for (int e = tid; e < kV * kH; e += kTfThreads) StabS[e] = p.Stab[e];
+  for (int e = tid; e < (kV + 1) * kH; e += kTfThreads) StabS[e] = e < kV * kH ? p.Stab[e] : 0.0f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -179,22 +181,27 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
     __syncthreads();   // SJ visible; D1 read by every thread before the next item's MMA
     // Gather addresses of sub-tile `sub` into address buffer `ab` (threads
     // gtid < 96 of the group; their global loads overlap the group's MMA).
+    // Per slot of sub-tile `sub`: the address of its V row (a decoded
+    // neighbour's PV row or the neighbour's PVenc row; a zero row for a slot
+    // past K, whose products the slot sum drops) and the offset of its W1c W_s
+    // row in shared memory (row 21 is zero).  Threads gtid < 96 of the group;
+    // their global loads overlap the group's MMA.
     auto stage = [&](int sub, int ab) {
       if (gtid < kSubN && sub * kSubRows < nseq) {
         const int s0 = sub * kSubRows;
         const int nrows = nseq - s0 < kSubRows ? nseq - s0 : kSubRows;
         const int rr = gtid / kK, k = gtid % kK;
-        int64_t src = -1;
-        int st = -1;
+        const uint16_t* src = g_zero_row;
+        int st = kV * kH;
         const int j = SJ[k];
         if (rr < nrows && j >= 0) {
           const int64_t qs = p.bv.seq_row_off[seq0 + s0 + rr];
           const int64_t qj = qs + j;
           if (p.pos[qj] < p.pos[qs + t]) {   // decoded neighbour: its own row
-            src = (l == 0 ? (int64_t)(off + j) : qj) * kH;
+            src = PVl + (l == 0 ? (int64_t)(off + j) : qj) * kH;
             st = p.tokens[qj] * kH;
           } else {                           // undecoded: the encoder row
-            src = ((int64_t)(off + j) * kH) | (1ll << 62);
+            src = p.PVenc + (int64_t)(off + j) * kH;
           }
         }
         SRC0[ab * kSubN + gtid] = src;
@@ -208,42 +215,35 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
       const int s0 = sub * kSubRows;
       const int nrows = nseq - s0 < kSubRows ? nseq - s0 : kSubRows;
       const int N = nrows * kK;
-      const int64_t* SRC = SRC0 + ab * kSubN;
-      const int* STR = STR0 + ab * kSubN;
+      const uint16_t* const* SRC = SRC0 + ab * kSubN + rho * kK;
+      const int* STR = STR0 + ab * kSubN + rho * kK;
       int64_t q = -1;
       if (rho < nrows) {
         const int64_t qs = p.bv.seq_row_off[seq0 + s0 + rho];
         q = qs + t;
         const float a = l == 0 ? p.Aenc0[(int64_t)r * kH + f] : p.A[q * kH + f];
+        // this thread's column of the SW128 operand: row (slot) k of this
+        // row's 48 is at gcol + (k / 8) * 1024 + (k % 8) * 128 + ((c ^ k % 8) << 4)
+        unsigned char* gcol = G + (f >> 6) * N * 128 + rho * kK * 128 + (f & 7) * 2;
+        const int c = (f & 63) >> 3;
+        const float* stf = StabS + f;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           // 24 slots: all gathers first, then the GELUs
           uint16_t raw[24];
 #pragma unroll
-          for (int u = 0; u < 24; ++u) {
-            const int64_t src = SRC[rho * kK + h * 24 + u];
-            raw[u] = 0;
-            if (src >= 0) {
-              const uint16_t* base = (src >> 62) ? p.PVenc : PVl;
-              raw[u] = base[(src & ~(1ll << 62)) + f];
-            }
-          }
+          for (int u = 0; u < 24; ++u) raw[u] = SRC[h * 24 + u][f];
 #pragma unroll
           for (int u = 0; u < 24; u += 2) {
-            float x[2];
-#pragma unroll
-            for (int w = 0; w < 2; ++w) {
-              const int st = STR[rho * kK + h * 24 + u + w];
-              x[w] = d1[h * 24 + u + w] + a + h2f(raw[u + w]) + (st >= 0 ? StabS[st + f] : 0.0f);
-            }
-            // the operand holds 2 GELU(x); the epilogue halves D2 (exact)
-            const float2 y = gelu2_tc_x2(make_float2(x[0], x[1]));
             const int k = h * 24 + u;
-            const bool v0 = SRC[rho * kK + k] >= 0, v1 = SRC[rho * kK + k + 1] >= 0;
-            *reinterpret_cast<__half*>(G + sw128_offset(rho * kK + k, f, N)) =
-                __float2half_rn(v0 ? y.x : 0.0f);
-            *reinterpret_cast<__half*>(G + sw128_offset(rho * kK + k + 1, f, N)) =
-                __float2half_rn(v1 ? y.y : 0.0f);
+            const float x0 = d1[k] + a + h2f(raw[u]) + stf[STR[k]];
+            const float x1 = d1[k + 1] + a + h2f(raw[u + 1]) + stf[STR[k + 1]];
+            // the operand holds 2 GELU(x); the epilogue halves D2 (exact)
+            const float2 y = gelu2_tc_x2(make_float2(x0, x1));
+            *reinterpret_cast<__half*>(gcol + (k >> 3) * 1024 + (k & 7) * 128 +
+                                       ((c ^ (k & 7)) << 4)) = __float2half_rn(y.x);
+            *reinterpret_cast<__half*>(gcol + ((k + 1) >> 3) * 1024 + ((k + 1) & 7) * 128 +
+                                       ((c ^ ((k + 1) & 7)) << 4)) = __float2half_rn(y.y);
           }
         }
       }
