@@ -1,7 +1,10 @@
 // Fused tcgen05 encoder-layer kernels for the tensor-core modes.  h_E is kept
-// in HBM as fp16 [R*48, 128] (slot s = residue * 48 + k) and every edge-wise
-// chain of an encoder layer runs in one pass over it, so no [R*48, 128]
-// intermediate ever goes to HBM:
+// in HBM as fp16 [R*48, 128] (slot s = residue * 48 + k) plus an fp16
+// remainder array of the same shape (h_E = hi + lo, about 22 significant
+// bits); MMAs read hi, the residual stream reads both.  Every edge-wise chain
+// of an encoder layer runs in one pass over h_E, so no [R*48, 128]
+// intermediate ever goes to HBM.  Weights are applied as fp16 value plus
+// fp16 remainder (two MMAs into one fp32 accumulator):
 //
 //   enc_node_tc  (proteinmpnn_encoder_scalar.cpp:169-243)
 //     D1 = W1b h_E                        M = 128 features, N = 192 slots
@@ -23,10 +26,11 @@
 //   enc_featurize_tc: edge features -> W_edge -> LN -> W_e, described below.
 //
 // All are persistent (one CTA per SM, 16 warps).  Weight images stay resident
-// in shared memory (bulk copies), the h_E tile of the next step is fetched by
-// cp.async into the second buffer while the current one is processed, and the
-// three (two) MMAs of a tile are issued by thread 0 and completion-tracked on
-// one mbarrier.  Every wait is bounded.
+// in shared memory (bulk copies; the edge pass streams its remainder images
+// through a 2-slot ring), the next tile's h_E rows are fetched by cp.async as
+// soon as the current tile's first MMA has read them, node terms are gathered
+// while MMAs run, and a tile's MMAs are issued by thread 0 and
+// completion-tracked on one mbarrier.  Every wait is bounded.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -211,6 +215,19 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       SA[tid] = att;
     }
     __syncthreads();
+    // node terms of this residue's slots: N_i and the first 16 slots' N_j,
+    // gathered while the D1 MMAs run (each 16-slot step loads the next 16)
+    const int r = t * kNodeRes + rho;
+    const float na = r < R ? p.NAC[(int64_t)r * 256 + f] : 0.0f;
+    float ncn[16];
+    auto load_nc = [&](int k0, float (&dst)[16]) {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int rj = SJ[rho * kK + k0 + k];
+        dst[k] = rj >= 0 ? p.NAC[(int64_t)rj * 256 + 128 + f] : 0.0f;
+      }
+    };
+    load_nc(0, ncn);
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
@@ -222,19 +239,20 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     cp_async_commit();
     // epilogue 1: G[slot][f] = GELU(D1 + N_i + N_j)  (16-bit stores, B layout),
     // 16 TMEM columns at a time
-    const int r = t * kNodeRes + rho;
-    const float na = r < R ? p.NAC[(int64_t)r * 256 + f] : 0.0f;
     unsigned char* G = sm + kNodeOffG;
-#pragma unroll 1
+#pragma unroll
     for (int k0 = 0; k0 < kK; k0 += 16) {
+      float ncc[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) ncc[k] = ncn[k];
+      if (k0 + 16 < kK) load_nc(k0 + 16, ncn);
       float v[16];
       tmem_ld16(tm + lane_base + (uint32_t)(rho * kK + k0), v);
 #pragma unroll
       for (int k = 0; k < 16; k += 2) {
         const int c = rho * kK + k0 + k;
         const int rj0 = SJ[c], rj1 = SJ[c + 1];
-        const float nc0 = rj0 >= 0 ? p.NAC[(int64_t)rj0 * 256 + 128 + f] : 0.0f;
-        const float nc1 = rj1 >= 0 ? p.NAC[(int64_t)rj1 * 256 + 128 + f] : 0.0f;
+        const float nc0 = ncc[k], nc1 = ncc[k + 1];
         const float2 y = gelu_tc_x2(make_float2(v[k] + na + nc0, v[k + 1] + na + nc1));
         *reinterpret_cast<__half*>(G + sw128_offset(c, f, kNodeSlots)) =
             __float2half_rn(rj0 >= 0 ? y.x : 0.0f);
@@ -398,6 +416,24 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       const int j = k < K ? p.e_idx[s] : -1;
       if (j >= 0 && j < L) rj = p.bv.prot_res_off[b] + j;
     }
+    // the slot's node terms [W11a h_i + b11] + W11c h_j on this thread's 32
+    // columns, gathered while the D1 MMAs run
+    float nsum[32];
+    if (rj >= 0) {
+      const float4* na = reinterpret_cast<const float4*>(p.NAC + (int64_t)r * 256 + c0);
+      const float4* nc = reinterpret_cast<const float4*>(p.NAC + (int64_t)rj * 256 + 128 + c0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 a = na[q], c = nc[q];
+        nsum[4 * q] = a.x + c.x;
+        nsum[4 * q + 1] = a.y + c.y;
+        nsum[4 * q + 2] = a.z + c.z;
+        nsum[4 * q + 3] = a.w + c.w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 32; ++q) nsum[q] = 0.0f;
+    }
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
@@ -415,17 +451,11 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       tmem_ld32(tm + lane_base + (uint32_t)c0, v);
       uint32_t pk[16];
       if (rj >= 0) {
-        const float4* na = reinterpret_cast<const float4*>(p.NAC + (int64_t)r * 256 + c0);
-        const float4* nc = reinterpret_cast<const float4*>(p.NAC + (int64_t)rj * 256 + 128 + c0);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 a = na[q], c = nc[q];
-          const float2 y01 = gelu_tc_x2(make_float2(v[4 * q + 0] + a.x + c.x,
-                                                    v[4 * q + 1] + a.y + c.y));
-          const float2 y23 = gelu_tc_x2(make_float2(v[4 * q + 2] + a.z + c.z,
-                                                    v[4 * q + 3] + a.w + c.w));
-          pk[2 * q] = pack_h2(y01.x, y01.y);
-          pk[2 * q + 1] = pack_h2(y23.x, y23.y);
+        for (int q = 0; q < 16; ++q) {
+          const float2 y = gelu_tc_x2(__fadd2_rn(make_float2(v[2 * q], v[2 * q + 1]),
+                                                 make_float2(nsum[2 * q], nsum[2 * q + 1])));
+          pk[q] = pack_h2(y.x, y.y);
         }
       } else {
 #pragma unroll
