@@ -826,9 +826,11 @@ __global__ void __launch_bounds__(kEncThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Decoder edge tables: PE_l = h_E W1b_l^T (l = 0..2, fp16 out) in one pass over
-// h_E -- the three decoder layers' h_E input blocks (decoder_layer_scalar.cpp:
-// 26-69 split by input block) share the A tile.
+// Decoder slot tables: PE_l = h_E W1b_l^T + PVenc_l[j] (l = 0..2, fp16 out) in
+// one pass over h_E -- the three decoder layers' h_E input blocks
+// (decoder_layer_scalar.cpp:26-69 split by input block) share the A tile, and
+// the epilogue adds the slot neighbour's fp16 W1d_l h_enc row (gathered while
+// the MMAs run) before the single rounding to fp16.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kTabOffW = 0;                            // 3 images
 constexpr uint32_t kTabOffA = 3 * kW128Bytes;               // 2 h_E tiles
@@ -892,10 +894,26 @@ __global__ void __launch_bounds__(kEncThreads, 1) dec_tables_tc_kernel(DecTables
     if (tn < tiles)
       load_rows_async(sm + kTabOffA + (buf ^ 1) * kEdgeTileBytes, p.h_e, tn * 128, SL, 128, tid);
     cp_async_commit();
+    // this thread's slot and its neighbour's residue row (-1: no neighbour)
+    const int64_t s = t * 128 + row;
+    int rj = -1;
+    if (s < SL) {
+      const int r = (int)(s / kK), k = (int)(s % kK);
+      const int b = p.bv.res_prot[r];
+      const int L = p.bv.prot_len[b];
+      const int j = k < (L < kK ? L : kK) ? p.e_idx[s] : -1;
+      if (j >= 0 && j < L) rj = p.bv.prot_res_off[b] + j;
+    }
+    uint4 pv[3][4];   // the three layers' PVenc rows, in flight during the MMA wait
+#pragma unroll
+    for (int l = 0; l < 3; ++l)
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        pv[l][u] = rj >= 0 ? ld_nc_noalloc_v4(p.PVenc[l] + (int64_t)rj * kH + c0 + 8 * u)
+                           : make_uint4(0, 0, 0, 0);
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
-    const int64_t s = t * 128 + row;
 #pragma unroll
     for (int l = 0; l < 3; ++l) {
       float v[32];
@@ -903,7 +921,11 @@ __global__ void __launch_bounds__(kEncThreads, 1) dec_tables_tc_kernel(DecTables
       if (s < SL) {
         uint32_t pk[16];
 #pragma unroll
-        for (int q = 0; q < 16; ++q) pk[q] = pack_h2(v[2 * q], v[2 * q + 1]);
+        for (int q = 0; q < 16; ++q) {
+          const uint32_t w = (&pv[l][q >> 2].x)[q & 3];
+          const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&w));
+          pk[q] = pack_h2(v[2 * q] + e.x, v[2 * q + 1] + e.y);
+        }
         uint4* dst = reinterpret_cast<uint4*>(p.out[l] + s * kH + c0);
 #pragma unroll
         for (int u = 0; u < 4; ++u)

@@ -441,8 +441,9 @@ bool build_stream_image(const std::map<std::string, TensorView>& t, bool f16,
     for (int i = 0; i < 4; ++i) {
       append_tile(*img, Wi, 128, 128 * i, 0);         // W_in rows 128i..128i+127
       append_tile(*img, Wi, 128, 128 * i, 0, true);   // and their remainder
-      append_tile(*img, Wo, 512, 0, 128 * i);         // W_out columns 128i..128i+127
     }
+    for (int i = 0; i < 4; ++i) append_tile(*img, Wo, 512, 0, 128 * i);   // W_out columns 128i..
+
   }
   return img->size() == (size_t)kStreamTilesPerStep * 128 * 128;
 }
@@ -864,12 +865,14 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
 }
 
 // Decoder tables straight to 16-bit (fp16 mode) for the fused decode kernel.
-hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const EncoderOut& eo,
-                             Bf16DecodeTables* tb, bool with_pe = true) {
+hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const BatchView& db_bv,
+                             const EncoderOut& eo, Bf16DecodeTables* tb, bool with_pe = true) {
   auto& ws = e->ws;
   cudaStream_t st = e->stream;
   const int64_t R = hb.R, SL = R * kK;
   DecTablesTcArgs ta;
+  ta.bv = db_bv;
+  ta.e_idx = eo.e_idx;
   ta.h_e = eo.h_e16;
   ta.rows = SL;
   ta.err = e->d_err;
@@ -879,6 +882,7 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const EncoderOu
     if ((with_pe && !pe) || !pv) return {HKB_UNAVAILABLE, "device allocation failed"};
     const std::string q = "dec" + std::to_string(l) + ".";
     ta.W[l] = e->gemm_img.at(q + "W1b");
+    ta.PVenc[l] = pv;
     ta.out[l] = pe;
     // W1d h_enc per residue, fp32 products rounded once to the 16-bit table
     gemm_f32x2(st, R, kH, kH, eo.h_v, kH, e->w32.dec[l].W1dT, kH, nullptr, 0, pv, kH, true);
@@ -953,8 +957,9 @@ hkb_status decode_f32(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
 }
 
 // bf16 mode: the fp32 decoder tables rounded to bf16.
-hkb_status decoder_tables_bf16(hkb_engine* e, const HostBatch& hb, const EncoderOut& eo,
-                               const DecoderTables& dt, Bf16DecodeTables* tb) {
+hkb_status decoder_tables_bf16(hkb_engine* e, const HostBatch& hb, const BatchView& db_bv,
+                               const EncoderOut& eo, const DecoderTables& dt,
+                               Bf16DecodeTables* tb) {
   auto& ws = e->ws;
   cudaStream_t st = e->stream;
   const int64_t R = hb.R, SL = R * kK;
@@ -962,8 +967,8 @@ hkb_status decoder_tables_bf16(hkb_engine* e, const HostBatch& hb, const Encoder
     uint16_t* pe = ws.get_as<uint16_t>("b.PE" + std::to_string(l), SL * kH);
     uint16_t* pv = ws.get_as<uint16_t>("b.PVenc" + std::to_string(l), R * kH);
     if (!pe || !pv) return {HKB_UNAVAILABLE, "device allocation failed"};
-    convert_f32_to_16(st, dt.PE[l], pe, SL * kH, false);
     convert_f32_to_16(st, dt.PVenc[l], pv, R * kH, false);
+    presum_slot_table(st, db_bv, eo.e_idx, dt.PE[l], pv, pe, false);
     tb->PE[l] = pe;
     tb->PVenc[l] = pv;
   }
@@ -1221,11 +1226,11 @@ hkb_status design_common(hkb_engine* e, const hkb_design_batch* batch,
   {
     PhaseRange r("hkb.decoder_tables");
     if (tc_encoder) {
-      s = decoder_tables_tc(e, *hb, eo, &tb);
+      s = decoder_tables_tc(e, *hb, db.bv, eo, &tb);
     } else {
       s = decoder_tables_f32(e, *hb, eo, &dt);
       if (s.code == HKB_OK && e->precision == HKB_PRECISION_BF16)
-        s = decoder_tables_bf16(e, *hb, eo, dt, &tb);
+        s = decoder_tables_bf16(e, *hb, db.bv, eo, dt, &tb);
     }
     if (s.code == HKB_OK) s = finish_orders(e, *hb, batch->decode_orders, out.orders);
   }
@@ -1301,7 +1306,7 @@ hkb_status score_tc(hkb_engine* e, const hkb_score_batch* batch, HostBatch& hb,
   HKB_CUDA(cudaEventRecord(e->ev[1], st));
   Bf16DecodeTables tb{};
   PhaseRange r_tab("hkb.decoder_tables+teacher_forced_layers");
-  s = decoder_tables_tc(e, hb, eo, &tb, /*with_pe=*/false);
+  s = decoder_tables_tc(e, hb, db.bv, eo, &tb, /*with_pe=*/false);
   if (s.code != HKB_OK) return s;
   if (!batch->orders) {
     s = finish_orders(e, hb, nullptr, d_orders);
@@ -1314,7 +1319,7 @@ hkb_status score_tc(hkb_engine* e, const hkb_score_batch* batch, HostBatch& hb,
   for (int l = 0; l < 3; ++l) {
     const std::string q = "dec" + std::to_string(l) + ".";
     // decode weight-stream tile of layer l: [W1a, W1d,] W2, W3, then
-    // 4 x (W_in, W_in remainder, W_out)
+    // 4 x (W_in, W_in remainder), then 4 x W_out
     auto tile = [](int layer, int i) { return stream_w2_tile(layer) + i; };
     TfSlotArgs sa;
     sa.bv = db.bv;
@@ -1347,7 +1352,11 @@ hkb_status score_tc(hkb_engine* e, const hkb_score_batch* batch, HostBatch& hb,
     na.S = S;
     na.stream = static_cast<const unsigned char*>(e->d_stream);
     na.tile_ids[0] = tile(l, 1);   // W3
-    for (int i = 0; i < 12; ++i) na.tile_ids[1 + i] = tile(l, 2 + i);
+    for (int i = 0; i < 4; ++i) {  // the node kernel consumes (W_in, remainder, W_out) per chunk
+      na.tile_ids[1 + 3 * i] = tile(l, 2 + 2 * i);
+      na.tile_ids[2 + 3 * i] = tile(l, 3 + 2 * i);
+      na.tile_ids[3 + 3 * i] = tile(l, 10 + i);
+    }
     if (l < 2) {
       na.tile_ids[13] = stream_w1a_tile(l + 1);       // W1a of layer l+1
       na.tile_ids[14] = stream_w1a_tile(l + 1) + 1;   // W1d of layer l+1

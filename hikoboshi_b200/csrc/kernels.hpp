@@ -172,15 +172,15 @@ int ar_f32_group_size();
 // Weight tiles for the fused decode kernel: every 128 x 128 operand tile is a
 // 16-bit image already in the SW128 K-major shared-memory layout, and the
 // tiles sit in the exact order the kernel consumes them in one decode position:
-//   layer 0: W2, W3, (W_in[i], W_in[i] remainder, W_out[:, i]) for i = 0..3
-//                                                                 (14 tiles)
-//   then for l = 1, 2: W1a_l, W1d_l, W2_l, W3_l, 4 x (W_in, W_in rem., W_out)
-//                                                                 (16 each)
+//   layer 0: W2, W3, (W_in[i], W_in[i] remainder) for i = 0..3, then
+//            W_out[:, i] for i = 0..3                             (14 tiles)
+//   then for l = 1, 2: W1a_l, W1d_l and the same 14               (16 each)
 // W_in is applied as hi + remainder (two MMAs into one accumulator): its
 // 16-bit rounding is the largest single error source of the decoder.
 constexpr int kStreamTilesPerStep = 46;
 // Stream tile index of layer l's W2 (its W1a and W1d sit just before it for
-// l > 0); W3 follows W2, then W_in[i] (hi, remainder) and W_out[:, i].
+// l > 0); W3 follows W2, then the four W_in[i] (hi, remainder) pairs and the
+// four W_out[:, i].
 __host__ __device__ constexpr int stream_w2_tile(int l) { return l == 0 ? 0 : 14 + 16 * (l - 1) + 2; }
 __host__ __device__ constexpr int stream_w1a_tile(int l) { return 14 + 16 * (l - 1); }
 constexpr int kTileBytes = 128 * 128 * 2;
@@ -208,8 +208,8 @@ struct Bf16DecodeWeights {
 };
 
 struct Bf16DecodeTables {
-  const uint16_t* PE[3];     // bf16 [R*48,128]
-  const uint16_t* PVenc[3];  // bf16 [R,128]
+  const uint16_t* PE[3];     // 16-bit [R*48,128] W1b_l h_E + PVenc_l[j] (DecTablesTcArgs)
+  const uint16_t* PVenc[3];  // 16-bit [R,128] W1d_l h_enc
   const float* Aenc0;        // [R,128]
   const float* h_enc;        // [R,128]
 };
@@ -292,10 +292,20 @@ struct EncFeatTcArgs {
 void launch_enc_featurize_tc(cudaStream_t st, const EncFeatTcArgs& p, int num_sms);
 
 // out[l] = h_E W[l]^T (fp16 [rows,128]) for three 128x128 images in one pass.
+// Decoder slot tables of the fused decode kernel, one per layer l:
+//   PE_l[s] = 16-bit(W1b_l h_E[s] + PVenc_l[j(s)])   (slot s = (residue, k))
+// i.e. the edge term plus the encoder-state neighbour term of slot s, with the
+// 16-bit PVenc_l row of the slot's neighbour j added in fp32 and the sum
+// rounded once.  A slot whose neighbour is undecoded (and every slot at layer
+// 0) reads only this row; a decoded neighbour adds the 16-bit correction
+// W1d_l h_j - PVenc_l[j] that the decode kernel stores when it decodes j.
 struct DecTablesTcArgs {
+  BatchView bv;
+  const int* e_idx = nullptr;            // [R,48]
   const uint16_t* h_e = nullptr;
   int64_t rows = 0;
   const unsigned char* W[3] = {nullptr, nullptr, nullptr};
+  const uint16_t* PVenc[3] = {nullptr, nullptr, nullptr};   // 16-bit [R,128]
   uint16_t* out[3] = {nullptr, nullptr, nullptr};
   unsigned int* err = nullptr;
 };
@@ -358,6 +368,10 @@ void launch_tf_rows(cudaStream_t st, const BatchView& bv, const int32_t* orders,
 int ar_tc_group_size();
 // f32 -> fp16 (f16 = true) or bf16, round to nearest even.
 void convert_f32_to_16(cudaStream_t st, const float* src, uint16_t* dst, int64_t n, bool f16);
+// bf16 engines: dst[s] = 16-bit(PE[s] + PVenc[j(s)]) from the fp32 edge table
+// (the slot tables of DecTablesTcArgs, built from fp32 products).
+void presum_slot_table(cudaStream_t st, const BatchView& bv, const int* e_idx, const float* PE,
+                       const uint16_t* PVenc, uint16_t* dst, bool f16);
 void launch_ar_decode_tc(cudaStream_t st, const BatchView& bv,
                          const Bf16DecodeWeights& w, const Bf16DecodeTables& t,
                          const ArBf16Args& a, bool f16, unsigned int* err);

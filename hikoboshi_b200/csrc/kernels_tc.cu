@@ -9,7 +9,12 @@
 // the activations as the B operand (N = sequences or neighbour slots on TMEM
 // columns):
 //   node terms   D_A = W1a h,  D_PV = W1d h          M=128 N=16  K=128
-//   messages     D2  = W2 GELU(A_t + W1b h_E + ...)   M=128 N=96  K=128 (x8 chunks)
+//   messages     D2  = W2 GELU(A_t + W1b h_E + W1d h_j + ...)
+//                                                     M=128 N=96  K=128 (x8 chunks)
+// W1b h_E + W1d h_enc_j is one precomputed 16-bit slot-table row per layer;
+// a decoded neighbour j adds the 16-bit correction W1d (h_j - h_enc_j) this
+// kernel stores when it decodes j, so an undecoded neighbour costs one
+// gathered row instead of two.
 //   aggregation  D3  = W3 (sum_k GELU(D2 + b2))       M=128 N=16  K=128
 //   FFN          DF  = W_in[i] h1,  DO += W_out[:, i] GELU(DF + b_in)  (i = 0..3)
 // W_in is applied as its fp16 value plus its fp16 remainder W_in - fp16(W_in)
@@ -54,20 +59,23 @@ constexpr uint32_t kColD2 = 0;    // 2 x 96
 constexpr uint32_t kColA = 192;
 constexpr uint32_t kColPV = 208;
 constexpr uint32_t kColD3 = 224;
-constexpr uint32_t kColDF = 240;
-constexpr uint32_t kColDF2 = 272;  // W_in remainder product (issued by a second thread)
-constexpr uint32_t kColDO = 256;
+constexpr uint32_t kColDO = 240;
+constexpr uint32_t kColDF = 256;   // 4 x 16: W_in[i] h1 (hi product), i = 0..3
+constexpr uint32_t kColDF2 = 320;  // 4 x 16: the W_in[i] remainder products
 constexpr uint32_t kTmemCols = 512;
 
 // Shared memory map (offsets from a 1024-byte aligned base)
-constexpr uint32_t kOffW = 0;                                   // 3 x 32 KiB
+constexpr uint32_t kOffW = 0;                                   // 4 x 32 KiB
 constexpr uint32_t kOffG1 = kOffW + kSlots * kTileBytes;        // 2 x 96 x 256 B
 constexpr uint32_t kG1Bytes = kChunkN * 256;
 constexpr uint32_t kOffHb = kOffG1 + 2 * kG1Bytes;              // [16,128] bf16
 constexpr uint32_t kOffSb = kOffHb + 4096;
 constexpr uint32_t kOffH1b = kOffSb + 4096;
-constexpr uint32_t kOffFb = kOffH1b + 4096;
-constexpr uint32_t kOffH = kOffFb + 4096;                       // fp32 [16,128]
+// The four FFN operands GELU(W_in[i] h1 + b_in[i]) ([16,128] each) live in the
+// first message operand buffer, which is idle from the last message MMA of a
+// layer to the first build of the next.
+constexpr uint32_t kOffFb = kOffG1;
+constexpr uint32_t kOffH = kOffH1b + 4096;                      // fp32 [16,128]
 constexpr uint32_t kOffAa = kOffH + kGB * kH * 4;
 constexpr uint32_t kOffXs = kOffAa + kGB * kH * 4;
 constexpr uint32_t kOffNb = kOffXs + kGB * kH * 4;              // int [16,48]
@@ -85,7 +93,8 @@ struct Misc {
   uint64_t bar_d2[2];     // message MMA of group g's chunk complete (D2 buffer g full)
   uint64_t bar_all;
   uint64_t bar_two;       // two issuing threads' MMAs complete (node terms)
-  uint64_t bar_ffn;       // three issuing threads' FFN MMAs complete
+  uint64_t bar_in[4];     // W_in[i] hi and remainder products complete (2 arrivals)
+  uint64_t bar_ffn;       // the four W_out products complete
   uint32_t tbase;
   int abort_flag;
   int t[kGB];
@@ -130,6 +139,12 @@ __device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
 template <bool F16>
 __device__ __forceinline__ uint16_t to16(float a) {
   return (uint16_t)(pack16<F16>(a, 0.0f) & 0xFFFFu);
+}
+
+template <bool F16>
+__device__ __forceinline__ float from16(uint16_t h) {
+  if constexpr (F16) return __half2float(__ushort_as_half(h));
+  else return __uint_as_float((uint32_t)h << 16);
 }
 
 // Instruction descriptor for fp16 (format 0) or bf16 (format 1) operands.
@@ -232,7 +247,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     mbar_init(&M.bar_d2[1], 1);
     mbar_init(&M.bar_all, 1);
     mbar_init(&M.bar_two, 2);
-    mbar_init(&M.bar_ffn, 3);
+    for (int i = 0; i < 4; ++i) mbar_init(&M.bar_in[i], 2);
+    mbar_init(&M.bar_ffn, 1);
     M.abort_flag = 0;
     fence_barrier_init();
   }
@@ -245,7 +261,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     M.off[tid] = live ? bv.prot_res_off[bv.seq_prot[sq]] : 0;
   }
   // Zero the small operand tiles once (rows of absent sequences stay zero).
-  for (int e = tid; e < 4 * 4096 / 16; e += kThreadsB)
+  for (int e = tid; e < 3 * 4096 / 16; e += kThreadsB)
     reinterpret_cast<uint4*>(sm + kOffHb)[e] = make_uint4(0, 0, 0, 0);
   if (warp == 0) {
     tmem_alloc(&M.tbase, kTmemCols);
@@ -279,7 +295,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   volatile int* abort_p = &M.abort_flag;
   uint4 raw_pe[kRowsPerThread], raw_v[kRowsPerThread];   // in-flight slot rows
   uint32_t d2_count = 0;   // this group's message MMAs waited for so far
-  uint32_t ph_all = 0, ph_two = 0, ph_ffn = 0;
+  uint32_t ph_all = 0, ph_two = 0, ph_ffn = 0, ph_in = 0;
   int tile = 0;   // next tile to consume (same on all threads)
 
   // The next position's h_enc / Aenc0 rows (residue t_next of each sequence)
@@ -365,14 +381,14 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     __syncthreads();
 
     // Row loads of one neighbour-slot chunk (a ping-pong group): a thread owns
-    // one 8-feature column chunk (tid % 16) of six slot rows (W1b h_E row and
-    // the neighbour's W1d h row, 16-bit).
+    // one 8-feature column chunk (tid % 16) of six slot rows: the slot table
+    // row (W1b h_E + W1d h_enc of the neighbour, 16-bit) and, for a decoded
+    // neighbour at layers 1 and 2, its correction row W1d (h_j - h_enc_j).
     auto load_rows = [&](int c, int layer, uint4 (&pe_raw)[kRowsPerThread],
                          uint4 (&v_raw)[kRowsPerThread]) {
       const int c8 = tid & 15;
       const int r0 = gtid >> 4;
       const uint16_t* PE = tb.PE[layer];
-      const uint16_t* PVenc = tb.PVenc[layer];
       const uint16_t* PVl =
           layer > 0 ? a.PV + (int64_t)(layer - 1) * a.total_rows * kH : nullptr;
 #pragma unroll
@@ -389,14 +405,14 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           pe_raw[i] = ld_nc_noalloc_v4(PE + (rt * kK + k) * kH + c8 * 8);
           if (bw && layer > 0)   // written by this kernel: coherent load
             v_raw[i] = ld_noalloc_v4(PVl + (M.qrow[s] + j) * kH + c8 * 8);
-          else
-            v_raw[i] = ld_nc_noalloc_v4(PVenc + (int64_t)(M.off[s] + j) * kH + c8 * 8);
         }
       }
     };
-    // GELU(A_t + W1b h_E + V + W1c W_s[tok]) into the SW128 operand of chunk c.
-    // The table terms are widened and added in fp32 (W1c W_s[tok] from the
-    // fp32 table in global memory, an L1-resident 10.5 KiB per layer).
+    // GELU(A_t + [W1b h_E + W1d h_enc_j] + dV + W1c W_s[tok]) into the SW128
+    // operand of chunk c, where dV = W1d (h_j - h_enc_j) for a decoded
+    // neighbour at layers 1 and 2 and 0 otherwise.  The table terms are
+    // widened and added in fp32 (W1c W_s[tok] from the fp32 table in global
+    // memory, an L1-resident 10.5 KiB per layer).
     auto build_operand = [&](int c, const float* StabL,
                              const uint4 (&pe_raw)[kRowsPerThread],
                              const uint4 (&v_raw)[kRowsPerThread]) {
@@ -455,27 +471,44 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           st.used = tile;                       // W1a, W1d of this layer released
           stream_issue(st, sm, M, w.stream);
         }
-        // warpgroups 0/1: A columns 0-7 / 8-15; warpgroups 2/3: PV columns
-        float v[8];
+        // warpgroups 0/1: A columns 0-7 / 8-15, needed by every build
         const int s0 = (wg & 1) * 8;
         if (wg < 2) {
+          float v[8];
           tmem_ld8(tm + lane_base + kColA + s0, v);
 #pragma unroll
           for (int q = 0; q < 8; ++q) Aa[s0 + q][feat] = v[q] + b1;
-        } else {
+        }
+        tc_fence_before();
+        __syncthreads();
+        // warpgroups 2/3 (the second message group, whose first chunk comes
+        // second): PV columns, W1d h of the current residues.  Later
+        // positions' backward slots read them as the correction to the slot
+        // table's encoder term, W1d h_t - PVenc[t] (16-bit).  Nothing at this
+        // position reads them and the next node MMA (end of this layer) is the
+        // first to overwrite the columns, so the stores stay off the first
+        // build's path.
+        if (wg >= 2) {
+          const uint16_t* PVe = tb.PVenc[l];
+          float e[8], v[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int s = s0 + q;
+            e[q] = s < n ? from16<F16>(PVe[(int64_t)(M.off[s] + M.t[s]) * kH + feat]) : 0.0f;
+          }
+          tc_fence_after();
           tmem_ld8(tm + lane_base + kColPV + s0, v);
           // Every decoded row is stored (the operand row of a masked residue
           // is zero, so its node term is exactly 0, as the reference's zeroed
-          // hidden state gives): PV needs no initialisation.
+          // hidden state gives; its h_enc row is zero too): PV needs no
+          // initialisation.
           uint16_t* PV = a.PV + (int64_t)(l - 1) * a.total_rows * kH;
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             const int s = s0 + q;
-            if (s < n) PV[(M.qrow[s] + M.t[s]) * kH + feat] = to16<F16>(v[q]);
+            if (s < n) PV[(M.qrow[s] + M.t[s]) * kH + feat] = to16<F16>(v[q] - e[q]);
           }
         }
-        tc_fence_before();
-        __syncthreads();
       }
       // ---- messages: gather + GELU -> W2 MMA -> GELU + slot sum ------------
       // Two ping-pong groups of 8 warps; group g takes chunks g, g+2, ... and
@@ -646,65 +679,66 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         }
       }
       // ---- FFN: DO = sum_i W_out[:, i] GELU(W_in[i] h1 + b_in[i]) ----------
-      // Three issuing threads: thread 0 W_in[i] (into DF), thread 32 its
-      // remainder (into DF2, summed in the epilogue), thread 64 W_out[:, i]
-      // (the only writer of DO, so its accumulation stays ordered).  After
-      // GELU(i) the three issue W_out[:, i], W_in[i+1] and its remainder side
-      // by side; each commits to bar_ffn (three arrivals per phase), so one
-      // wait covers W_in[i+1] and W_out[:, i], which frees Fb for GELU(i+1).
-      if (tid == 0 || tid == 32 || tid == 64) {
-        if (tid != 64) {
-          const uint32_t wa = stream_wait(tid == 0 ? tile : tile + 1, sm, M, err);
+      // The stream holds W_in[0..3] (hi, remainder) and then W_out[:, 0..3],
+      // so the eight W_in products never wait for a GELU: thread 0 issues the
+      // hi products, thread 32 the remainder products, chunk i into its own
+      // TMEM columns, each pair completing bar_in[i].  Round 1 issues chunks
+      // 0 and 1 (their tiles are resident by now), round 2 chunks 2 and 3
+      // (their tiles load as chunks 0 and 1 complete), and every thread
+      // applies GELU(i) as soon as bar_in[i] completes; after one barrier
+      // thread 0 issues the four W_out products into DO.
+      auto issue_in = [&](int i) {
+        if (tid == 0 || tid == 32) {
+          const int lo = tid == 32;
+          const uint32_t wa = stream_wait(tile + 2 * i + lo, sm, M, err);
           tc_fence_after();
           if (!*abort_p)
-            mma_k128(tm + (tid == 0 ? kColDF : kColDF2), wa, smem_u32(sm + kOffH1b), kGB,
+            mma_k128(tm + (lo ? kColDF2 : kColDF) + 16 * i, wa, smem_u32(sm + kOffH1b), kGB,
                      idesc16<F16>(128, kGB), false);
+          mma_commit(&M.bar_in[i]);
+        }
+      };
+      auto gelu_in = [&](int i, float bi) {
+        if (!mbar_wait(&M.bar_in[i], ph_in, err)) *abort_p = 1;
+        tc_fence_after();
+        if (tid == 0) {
+          st.used = tile + 2 * (i + 1);         // W_in[0..i] and remainders consumed
+          stream_issue(st, sm, M, w.stream);
+        }
+        float v[4], v2[4];
+        tmem_ld4(tm + lane_base + kColDF + 16 * i + wg * 4, v);
+        tmem_ld4(tm + lane_base + kColDF2 + 16 * i + wg * 4, v2);
+        unsigned char* fb = sm + kOffFb + i * 4096;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int s = wg * 4 + q;
+          const float y = s < n ? gelu_tc((v[q] + v2[q]) + bi) : 0.0f;
+          *reinterpret_cast<uint16_t*>(fb + sw128_offset(s, feat, kGB)) = to16<F16>(y);
+        }
+      };
+      issue_in(0);
+      issue_in(1);
+      gelu_in(0, b_in0);
+      gelu_in(1, b_in1);
+      issue_in(2);
+      issue_in(3);
+      gelu_in(2, b_in2);
+      gelu_in(3, b_in3);
+      ph_in ^= 1;
+      fence_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t wa = stream_wait(tile + 8 + i, sm, M, err);   // W_out[:, i]
+          tc_fence_after();
+          if (!*abort_p)
+            mma_k128(tm + kColDO, wa, smem_u32(sm + kOffFb + i * 4096), kGB,
+                     idesc16<F16>(128, kGB), i > 0);
         }
         mma_commit(&M.bar_ffn);
       }
-      tile += 2;                                // W_in[0] and its remainder
-      for (int i = 0; i < 4; ++i) {
-        if (!mbar_wait(&M.bar_ffn, ph_ffn, err)) *abort_p = 1;
-        ph_ffn ^= 1;
-        tc_fence_after();
-        if (tid == 0) {
-          st.used = tile;                       // every tile before W_out[:, i] is consumed
-          stream_issue(st, sm, M, w.stream);
-        }
-        {
-          float v[4], v2[4];
-          tmem_ld4(tm + lane_base + kColDF + wg * 4, v);
-          tmem_ld4(tm + lane_base + kColDF2 + wg * 4, v2);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) v[q] += v2[q];
-          const float bi = i == 0 ? b_in0 : i == 1 ? b_in1 : i == 2 ? b_in2 : b_in3;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int s = wg * 4 + q;
-            const float y = s < n ? gelu_tc(v[q] + bi) : 0.0f;
-            *reinterpret_cast<uint16_t*>(sm + kOffFb + sw128_offset(s, feat, kGB)) = to16<F16>(y);
-          }
-        }
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0 || tid == 32 || tid == 64) {
-          if (tid == 64) {
-            const uint32_t wa = stream_wait(tile, sm, M, err);          // W_out[:, i]
-            tc_fence_after();
-            if (!*abort_p)
-              mma_k128(tm + kColDO, wa, smem_u32(sm + kOffFb), kGB, idesc16<F16>(128, kGB), i > 0);
-          } else if (i < 3) {
-            const uint32_t wa = stream_wait(tid == 0 ? tile + 1 : tile + 2, sm, M, err);
-            tc_fence_after();
-            if (!*abort_p)
-              mma_k128(tm + (tid == 0 ? kColDF : kColDF2), wa, smem_u32(sm + kOffH1b), kGB,
-                       idesc16<F16>(128, kGB), false);
-          }
-          mma_commit(&M.bar_ffn);
-        }
-        tile += i < 3 ? 3 : 1;                  // W_out[:, i] (and W_in[i+1], remainder)
-      }
+      tile += 12;
       if (!mbar_wait(&M.bar_ffn, ph_ffn, err)) *abort_p = 1;
       ph_ffn ^= 1;
       tc_fence_after();
@@ -858,6 +892,41 @@ __global__ void f32_to_16_kernel(const float* __restrict__ src, uint16_t* __rest
 }  // namespace
 
 int ar_tc_group_size() { return kGB; }
+
+// One thread per (slot, 8-feature chunk): dst = 16-bit(PE + PVenc[neighbour]).
+template <bool F16>
+__global__ void presum_slot_table_kernel(const BatchView bv, const int* __restrict__ e_idx,
+                                         const float* __restrict__ PE,
+                                         const uint16_t* __restrict__ PVenc,
+                                         uint16_t* __restrict__ dst, int64_t units) {
+  const int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= units) return;
+  const int64_t s = u >> 4;
+  const int c = (int)(u & 15) * 8;
+  const int r = (int)(s / kK), k = (int)(s % kK);
+  const int b = bv.res_prot[r];
+  const int L = bv.prot_len[b];
+  const int j = k < (L < kK ? L : kK) ? e_idx[s] : -1;
+  const int rj = (j >= 0 && j < L) ? bv.prot_res_off[b] + j : -1;
+  float x[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    x[i] = PE[s * kH + c + i];
+    if (rj >= 0) x[i] += from16<F16>(PVenc[(int64_t)rj * kH + c + i]);
+  }
+  *reinterpret_cast<uint4*>(dst + s * kH + c) =
+      make_uint4(pack16<F16>(x[0], x[1]), pack16<F16>(x[2], x[3]), pack16<F16>(x[4], x[5]),
+                 pack16<F16>(x[6], x[7]));
+}
+
+void presum_slot_table(cudaStream_t st, const BatchView& bv, const int* e_idx, const float* PE,
+                       const uint16_t* PVenc, uint16_t* dst, bool f16) {
+  const int64_t units = (int64_t)bv.total_residues * kK * 16;
+  if (units <= 0) return;
+  const unsigned grid = (unsigned)((units + 255) / 256);
+  if (f16) presum_slot_table_kernel<true><<<grid, 256, 0, st>>>(bv, e_idx, PE, PVenc, dst, units);
+  else presum_slot_table_kernel<false><<<grid, 256, 0, st>>>(bv, e_idx, PE, PVenc, dst, units);
+}
 
 void convert_f32_to_16(cudaStream_t st, const float* src, uint16_t* dst, int64_t n, bool f16) {
   if (n <= 0) return;
