@@ -10,7 +10,7 @@
 // columns):
 //   node terms   D_A = W1a h,  D_PV = W1d h          M=128 N=16  K=128
 //   messages     D2  = W2 GELU(A_t + W1b h_E + W1d h_j + ...)
-//                                                     M=128 N=96  K=128 (x8 chunks)
+//                                                     M=128 N=48  K=128 (per sequence)
 // W1b h_E + W1d h_enc_j is one precomputed 16-bit slot-table row per layer;
 // a decoded neighbour j adds the 16-bit correction W1d (h_j - h_enc_j) this
 // kernel stores when it decodes j, so an undecoded neighbour costs one
@@ -21,17 +21,18 @@
 // (two products summed in fp32: about twice the 16-bit precision for the
 // decoder's most error-sensitive weight).  The slot sum runs along a thread's
 // own TMEM row, LayerNorm statistics are warp reductions over a transposed
-// fp32 copy, and the sampler is the reference's (serial over 21 logits,
-// double CDF).
+// fp32 copy, the logits are a warp per sequence, and the sampler is the
+// reference's (double CDF).
 //
 // Weight tiles stream through a 4-slot shared-memory ring by 1-D bulk copies
 // (no tensor map) issued by thread 0 in consumption order; independent MMAs
-// of the node and FFN phases are issued by up to three threads.  The CTA has
-// 16 warps.  In the message (slot) phase they form two ping-pong groups of 8
-// warps; each group gathers the neighbour rows of its next chunk (in
-// registers, one chunk ahead), builds the GELU operand, issues the MMA and
-// sums GELU(D2 + b2) over the slots of its own chunks, so that one group's
-// MMA wait and slot sum overlap the other group's gather and build.  All 16
+// of the node and FFN phases are issued by two threads.  The per-layer
+// W1c W_s table is staged in shared memory by a bulk copy.  The CTA has 16
+// warps.  In the message (slot) phase they form four groups of 4 warps; each
+// group gathers the neighbour rows of its next sequence (in registers, one
+// chunk ahead), builds the GELU operand, issues the MMA and sums
+// GELU(D2 + b2) over the slots of its own sequences, so that one group's MMA
+// wait and slot sum overlap the other groups' gathers and builds.  All 16
 // warps share the node, LayerNorm, FFN and sampling phases.  Every wait is
 // bounded; a timeout sets the error word and the CTA stops.
 #include <cuda_bf16.h>
@@ -47,28 +48,40 @@ namespace {
 using namespace tc;
 
 constexpr int kGB = 16;           // sequences per CTA
-constexpr int kChunkSeqs = 2;     // sequences per message MMA
-constexpr int kChunkN = kChunkSeqs * kK;  // 96 neighbour slots
+// Message-phase groups: four groups of 4 warps, each owning one-sequence
+// chunks (48 slots), measured slightly faster than two groups of 8 warps with
+// two-sequence chunks (the other supported setting).
+#ifndef HKB_MSG_GROUPS
+#define HKB_MSG_GROUPS 4
+#endif
+constexpr int kGroups = HKB_MSG_GROUPS;   // message-phase groups (2 or 4)
+constexpr int kChunkSeqs = 4 / kGroups;   // sequences per message MMA
+constexpr int kChunkN = kChunkSeqs * kK;  // neighbour slots per message MMA
 constexpr int kSlots = 4;         // weight ring depth
 constexpr int kThreadsB = 512;
 constexpr int kWarpsB = kThreadsB / 32;
-constexpr int kGroupThreads = 256;  // message-phase ping-pong group: warps 0-7 / 8-15
+constexpr int kGroupThreads = kThreadsB / kGroups;   // threads of a message group
+static_assert(kGroups * kChunkN * 256 == 2 * 96 * 256, "message operand buffers");
 
 // TMEM columns (fp32 accumulators, lanes = output features)
-constexpr uint32_t kColD2 = 0;    // 2 x 96
-constexpr uint32_t kColA = 192;
-constexpr uint32_t kColPV = 208;
-constexpr uint32_t kColD3 = 224;
-constexpr uint32_t kColDO = 240;
-constexpr uint32_t kColDF = 256;   // 4 x 16: W_in[i] h1 (hi product), i = 0..3
-constexpr uint32_t kColDF2 = 320;  // 4 x 16: the W_in[i] remainder products
+// (group g's message accumulator at kColD2 + g * kD2Stride: 96-column
+// chunks sit back to back, 48-column ones on 64-column boundaries)
+constexpr uint32_t kD2Stride = kChunkN == 96 ? 96 : 64;
+constexpr uint32_t kColD2 = 0;
+constexpr uint32_t kColA = kColD2 + kGroups * kD2Stride;
+constexpr uint32_t kColPV = kColA + 16;
+constexpr uint32_t kColD3 = kColPV + 16;
+constexpr uint32_t kColDO = kColD3 + 16;
+constexpr uint32_t kColDF = kColDO + 16;   // 4 x 16: W_in[i] h1 (hi product), i = 0..3
+constexpr uint32_t kColDF2 = kColDF + 64;  // 4 x 16: the W_in[i] remainder products
 constexpr uint32_t kTmemCols = 512;
+static_assert(kColDF2 + 64 <= kTmemCols, "tensor memory columns");
 
 // Shared memory map (offsets from a 1024-byte aligned base)
 constexpr uint32_t kOffW = 0;                                   // 4 x 32 KiB
 constexpr uint32_t kOffG1 = kOffW + kSlots * kTileBytes;        // 2 x 96 x 256 B
 constexpr uint32_t kG1Bytes = kChunkN * 256;
-constexpr uint32_t kOffHb = kOffG1 + 2 * kG1Bytes;              // [16,128] bf16
+constexpr uint32_t kOffHb = kOffG1 + kGroups * kG1Bytes;        // [16,128] bf16
 constexpr uint32_t kOffSb = kOffHb + 4096;
 constexpr uint32_t kOffH1b = kOffSb + 4096;
 // The four FFN operands GELU(W_in[i] h1 + b_in[i]) ([16,128] each) live in the
@@ -77,24 +90,30 @@ constexpr uint32_t kOffH1b = kOffSb + 4096;
 constexpr uint32_t kOffFb = kOffG1;
 constexpr uint32_t kOffH = kOffH1b + 4096;                      // fp32 [16,128]
 constexpr uint32_t kOffAa = kOffH + kGB * kH * 4;
-constexpr uint32_t kOffXs = kOffAa + kGB * kH * 4;
-constexpr uint32_t kOffNb = kOffXs + kGB * kH * 4;              // int [16,48]
-constexpr uint32_t kOffLogit = kOffNb + kGB * kK * 4;           // float [16,32]
-// The W1c.W_s tables (fp32 [3][21][128]) and the logit head (fp32, transposed
-// with a padded pitch) are read from global memory through L1: shared memory
-// goes to the fourth weight-ring slot.
-constexpr uint32_t kOffNbNext = kOffLogit + kGB * 32 * 4;       // int [16,48] next position
+// The residual of LayerNorm 1 (fp32 [16,128]) lives in the second message
+// operand buffer, idle from the last message MMA of a layer to the first
+// build of the next (it is written after W3 and last read at LayerNorm 2).
+constexpr uint32_t kOffXs = kOffG1 + 4 * 4096;
+// W1c_l W_s (fp32 [21,128]) of the current layer, staged by one bulk copy
+// after the previous layer's last build.
+constexpr uint32_t kStabBytes = kV * kH * 4;
+constexpr uint32_t kOffStab = kOffAa + kGB * kH * 4;
+constexpr uint32_t kOffNb = kOffStab + kStabBytes;              // int [16,48]
+// The logit head (fp32, transposed with a padded pitch) is read from global
+// memory through L1.
+constexpr uint32_t kOffNbNext = kOffNb + kGB * kK * 4;          // int [16,48] next position
 constexpr uint32_t kOffMisc = kOffNbNext + kGB * kK * 4;
 constexpr uint32_t kSmemBytes = kOffMisc + 1024 + 1024;         // + misc + alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "decode kernel shared memory");
 
 struct Misc {
   uint64_t full[kSlots];
-  uint64_t bar_d2[2];     // message MMA of group g's chunk complete (D2 buffer g full)
+  uint64_t bar_d2[kGroups];   // message MMA of group g's chunk complete (D2 buffer g full)
   uint64_t bar_all;
   uint64_t bar_two;       // two issuing threads' MMAs complete (node terms)
   uint64_t bar_in[4];     // W_in[i] hi and remainder products complete (2 arrivals)
   uint64_t bar_ffn;       // the four W_out products complete
+  uint64_t bar_stab;      // the next layer's W1c W_s table has landed
   uint32_t tbase;
   int abort_flag;
   int t[kGB];
@@ -206,7 +225,6 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   float (*Xs)[kH] = reinterpret_cast<float (*)[kH]>(sm + kOffXs);
   int (*Nb)[kK] = reinterpret_cast<int (*)[kK]>(sm + kOffNb);
   int (*NbNext)[kK] = reinterpret_cast<int (*)[kK]>(sm + kOffNbNext);
-  float (*Lg)[32] = reinterpret_cast<float (*)[32]>(sm + kOffLogit);
   const float* HeadS = w.headP;
 
   const int tid = threadIdx.x;
@@ -243,12 +261,12 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
 
   if (tid == 0) {
     for (int i = 0; i < kSlots; ++i) mbar_init(&M.full[i], 1);
-    mbar_init(&M.bar_d2[0], 1);
-    mbar_init(&M.bar_d2[1], 1);
+    for (int i = 0; i < kGroups; ++i) mbar_init(&M.bar_d2[i], 1);
     mbar_init(&M.bar_all, 1);
     mbar_init(&M.bar_two, 2);
     for (int i = 0; i < 4; ++i) mbar_init(&M.bar_in[i], 2);
     mbar_init(&M.bar_ffn, 1);
+    mbar_init(&M.bar_stab, 1);
     M.abort_flag = 0;
     fence_barrier_init();
   }
@@ -274,6 +292,18 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
 
   Stream st{0, 0, L * kStreamTilesPerStep};
   if (tid == 0) stream_issue(st, sm, M, w.stream);
+  // W1c_l W_s staging: one copy in flight at most, issued by thread 0 after
+  // every build of the layer before it (layer 0 of position 0: here).
+  auto stab_issue = [&](int layer) {
+    mbar_arrive_expect_tx(&M.bar_stab, kStabBytes);
+    bulk_g2s(sm + kOffStab, w.Stab[layer], kStabBytes, &M.bar_stab);
+  };
+  bool stab_pending = false;   // thread 0: a staging copy not yet waited for
+  uint32_t ph_stab = 0;
+  if (tid == 0) {
+    stab_issue(0);
+    stab_pending = true;
+  }
 
   // decode positions of every residue of this CTA's sequences
   for (int s = 0; s < n; ++s)
@@ -291,7 +321,12 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
   constexpr int kRowsPerThread = kChunkN * 16 / kGroupThreads;
   const int grp = tid / kGroupThreads;       // ping-pong group of the message phase
   const int gtid = tid % kGroupThreads;
-  const int sub = (warp >> 2) & 1;           // sequence of a chunk this warp sums
+  // sequence of a chunk this warp sums (two-sequence chunks: warps 4-7 of a
+  // group take the second)
+  const int sub = kChunkSeqs == 2 ? (warp >> 2) & 1 : 0;
+  constexpr int kRowStride = kGroupThreads / 16;   // slot rows between a thread's rows
+  // message-phase chunks (two sequences each): group g takes g, g+2, ...
+  const int nch = (n + kChunkSeqs - 1) / kChunkSeqs;
   volatile int* abort_p = &M.abort_flag;
   uint4 raw_pe[kRowsPerThread], raw_v[kRowsPerThread];   // in-flight slot rows
   uint32_t d2_count = 0;   // this group's message MMAs waited for so far
@@ -393,7 +428,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           layer > 0 ? a.PV + (int64_t)(layer - 1) * a.total_rows * kH : nullptr;
 #pragma unroll
       for (int i = 0; i < kRowsPerThread; ++i) {
-        const int r = r0 + 16 * i;
+        const int r = r0 + kRowStride * i;
         const int s = c * kChunkSeqs + r / kK, k = r % kK;
         pe_raw[i] = make_uint4(0, 0, 0, 0);
         v_raw[i] = make_uint4(0, 0, 0, 0);
@@ -411,17 +446,17 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     // GELU(A_t + [W1b h_E + W1d h_enc_j] + dV + W1c W_s[tok]) into the SW128
     // operand of chunk c, where dV = W1d (h_j - h_enc_j) for a decoded
     // neighbour at layers 1 and 2 and 0 otherwise.  The table terms are
-    // widened and added in fp32 (W1c W_s[tok] from the fp32 table in global
-    // memory, an L1-resident 10.5 KiB per layer).
+    // widened and added in fp32 (W1c W_s[tok] from the layer's fp32 table in
+    // shared memory).
     auto build_operand = [&](int c, const float* StabL,
                              const uint4 (&pe_raw)[kRowsPerThread],
                              const uint4 (&v_raw)[kRowsPerThread]) {
-      unsigned char* dst = sm + kOffG1 + (c & 1) * kG1Bytes;
+      unsigned char* dst = sm + kOffG1 + grp * kG1Bytes;
       const int c8 = tid & 15;
       const int r0 = gtid >> 4;
 #pragma unroll
       for (int i = 0; i < kRowsPerThread; ++i) {
-        const int r = r0 + 16 * i;
+        const int r = r0 + kRowStride * i;
         const int s = c * kChunkSeqs + r / kK, k = r % kK;
         uint4 outv = make_uint4(0, 0, 0, 0);
         if (s < n && k < K) {
@@ -434,8 +469,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
           if (bw) {
             const float4* st = reinterpret_cast<const float4*>(StabL + tok * kH) + c8 * 2;
-            s0 = __ldg(st);
-            s1 = __ldg(st + 1);
+            s0 = st[0];
+            s1 = st[1];
           }
           const float st8[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
           const float4 a0 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2];
@@ -520,7 +555,6 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       // the slots.  While one group waits on its MMA or sums, the other
       // builds, so the two halves of the work overlap without handing
       // buffers across groups.
-      const int nch = (n + kChunkSeqs - 1) / kChunkSeqs;
       {
         // The PE rows (W1b h_E: K contiguous rows per sequence) of the next
         // message phase -- layer l+1 here, or layer 0 at the next position --
@@ -532,13 +566,16 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           bulk_prefetch_l2(tb.PE[l < 2 ? l + 1 : 0] + (int64_t)(M.off[gtid] + t) * kK * kH,
                            (uint32_t)(K * kH * 2));
         }
-        const float* StabL = w.Stab[l];
+        if (mbar_wait(&M.bar_stab, ph_stab, err)) stab_pending = false;
+        else *abort_p = 1;
+        ph_stab ^= 1;
+        const float* StabL = reinterpret_cast<const float*>(sm + kOffStab);
         const float2 half2c = make_float2(0.5f, 0.5f);
         const float b2 = w.b2[l][feat];
         const float2 b2p = make_float2(b2, b2);
-        const uint32_t d2col = kColD2 + grp * kChunkN + sub * kK;
+        const uint32_t d2col = kColD2 + grp * kD2Stride + sub * kK;
         uint32_t wa = 0;
-        for (int c = grp; c < nch; c += 2) {
+        for (int c = grp; c < nch; c += kGroups) {
           // Operand / D2 buffer grp is free: this group waited for its last
           // MMA and read its D2 before arriving at the barrier below.
           build_operand(c, StabL, raw_pe, raw_v);
@@ -548,12 +585,12 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
             if (c == grp) wa = stream_wait(tile, sm, M, err);
             tc_fence_after();
             if (!*abort_p)
-              mma_k128(tm + kColD2 + grp * kChunkN, wa,
+              mma_k128(tm + kColD2 + grp * kD2Stride, wa,
                        smem_u32(sm + kOffG1 + grp * kG1Bytes), kChunkN,
                        idesc16<F16>(128, kChunkN), false);
             mma_commit(&M.bar_d2[grp]);
           }
-          if (c + 2 < nch) load_rows(c + 2, l, raw_pe, raw_v);
+          if (c + kGroups < nch) load_rows(c + kGroups, l, raw_pe, raw_v);
           else if (l < 2) load_rows(grp, l + 1, raw_pe, raw_v);
           if (!*abort_p && !mbar_wait_abortable(&M.bar_d2[grp], d2_count & 1, err, abort_p))
             *abort_p = 1;
@@ -600,6 +637,11 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       }
       ++tile;                                   // W2 consumed
       __syncthreads();
+      // every build of this layer is done: stage the next layer's table
+      if (tid == 0 && (l < 2 || p + 1 < L) && !*abort_p) {
+        stab_issue(l < 2 ? l + 1 : 0);
+        stab_pending = true;
+      }
       // ---- W3 after the slot sum, residual + LayerNorm 1 --------------------
       // This layer's epilogue biases, loaded while the W3 MMA runs (a load
       // issued after an MMA wait would put its latency on the critical path).
@@ -649,10 +691,11 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       }
       fence_async_smem();
       __syncthreads();
-      // ---- last layer: the next position's neighbour codes (its residue and
-      // mask were read at this position's set-up) and an L2 prefetch of its
-      // node rows; they are consumed after this position's sampling.
-      if (l == 2 && p + 1 < L) {
+      // ---- layer 0, while the first W_in products run: the next position's
+      // neighbour codes (its residue and mask were read at this position's
+      // set-up) and an L2 prefetch of its node rows; they are consumed after
+      // this position's sampling.
+      auto next_codes = [&]() {
         for (int e = tid; e < n * kK; e += kThreadsB) {
           const int s = e / kK, k = e % kK;
           int code = 0;
@@ -677,7 +720,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
                              (int64_t)(M.off[s] + M.t_next[s]) * kH + line * 32;
           asm volatile("prefetch.global.L2 [%0];" ::"l"(row));
         }
-      }
+      };
       // ---- FFN: DO = sum_i W_out[:, i] GELU(W_in[i] h1 + b_in[i]) ----------
       // The stream holds W_in[0..3] (hi, remainder) and then W_out[:, 0..3],
       // so the eight W_in products never wait for a GELU: thread 0 issues the
@@ -718,6 +761,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       };
       issue_in(0);
       issue_in(1);
+      if (l == 0 && p + 1 < L) next_codes();
       gelu_in(0, b_in0);
       gelu_in(1, b_in1);
       issue_in(2);
@@ -793,32 +837,40 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     // Aa is free from here to the next position's set-up
     if (p + 1 < L) stage_next_rows(Aa, tb.Aenc0);
     // ---- logits and sampling ------------------------------------------------
-    for (int e = tid; e < kGB * kV; e += kThreadsB) {
-      const int s = e / kV, v = e % kV;
-      float z = 0.0f;
-      if (s < n) {
-        z = w.head_b[v];
-        const float4* hr = reinterpret_cast<const float4*>(hS[s]);
-        const float4* wr = reinterpret_cast<const float4*>(HeadS + v * kHeadPitch);   // L1
-#pragma unroll 8
-        for (int f4 = 0; f4 < kH / 4; ++f4) {   // same fma order as f = 0..127
-          const float4 h = hr[f4], wv = wr[f4];
-          z = fmaf(h.x, wv.x, z);
-          z = fmaf(h.y, wv.y, z);
-          z = fmaf(h.z, wv.z, z);
-          z = fmaf(h.w, wv.w, z);
-        }
-      }
-      Lg[s][v] = z;
-    }
-    __syncthreads();
-    if (p + 1 < L) stage_next_rows(hS, tb.h_enc);   // hS is no longer read
-    // One warp per sequence, one lane per vocabulary entry
+    // One warp per sequence (kGB == kWarpsB).  Lane i holds features
+    // 4i..4i+3 of h and forms its partial dot products with the 21 head rows
+    // (coalesced 512-byte row reads); a reduce-scatter over the warp (five
+    // butterfly levels, each lane keeping half of its values) leaves lane v
+    // with the full product for vocabulary entry v.  Then
     // (sampler_scalar.cpp:49-92): temperature-scaled log-softmax emitted as
     // the log-prob row, then greedy argmax (first maximum) or one uniform draw
     // against the double-precision CDF.  Sums run as warp reductions, so they
     // differ from the serial order by rounding only.
-    for (int s = warp; s < n; s += kWarpsB) {
+    static_assert(kGB == kWarpsB, "one warp per sequence");
+    if (warp < n) {
+      const int s = warp;
+      float zp[32];
+      {
+        const float4 h = reinterpret_cast<const float4*>(hS[s])[lane];
+#pragma unroll
+        for (int v = 0; v < 32; ++v) {
+          zp[v] = 0.0f;
+          if (v < kV) {
+            const float4 wv = reinterpret_cast<const float4*>(HeadS + v * kHeadPitch)[lane];
+            zp[v] = fmaf(h.w, wv.w, fmaf(h.z, wv.z, fmaf(h.y, wv.y, h.x * wv.x)));
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < o; ++i) {
+          const float send = up ? zp[i] : zp[i + o];
+          const float keep = up ? zp[i + o] : zp[i];
+          zp[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
       const int t = M.t[s];
       const int64_t q = M.qrow[s] + t;
       float* lp = a.log_probs + q * kV;
@@ -830,7 +882,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         const float temperature = M.temp[s];
         const bool greedy = !(temperature > 0.0f);
         const float T = (temperature > 0.0f && isfinite(temperature)) ? temperature : 1.0f;
-        const float z = in_vocab ? Lg[s][lane] / T : -INFINITY;
+        const float z = in_vocab ? (w.head_b[lane] + zp[0]) / T : -INFINITY;
         const float mx = warp_max(z);
         const float e = in_vocab ? expf(z - mx) : 0.0f;
         const float sum = warp_sum(e);
@@ -862,11 +914,15 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         M.tok_cur[s] = tok;
       }
     }
+    // Warp w stages row w, the row it alone read above.
+    __syncwarp();
+    if (p + 1 < L) stage_next_rows(hS, tb.h_enc);
     __syncthreads();
   }
   cp_async_wait_all();   // staged rows of a position an abort skipped
   // Drain: no bulk copy may still be in flight when the CTA exits.
   if (tid == 0) {
+    if (stab_pending) mbar_wait(&M.bar_stab, ph_stab, err);
     for (int j = tile; j < st.issued; ++j) {
       const int slot = j % kSlots;
       mbar_wait(&M.full[slot], (uint32_t)((j / kSlots) & 1), err);
