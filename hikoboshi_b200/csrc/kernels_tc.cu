@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
 
   // a group thread owns one 8-feature column chunk of this many slot rows
   constexpr int kRowsPerThread = kChunkN * 16 / kGroupThreads;
-  const int grp = tid / kGroupThreads;       // ping-pong group of the message phase
+  const int grp = tid / kGroupThreads;       // message-phase group
   const int gtid = tid % kGroupThreads;
   // sequence of a chunk this warp sums (two-sequence chunks: warps 4-7 of a
   // group take the second)
@@ -415,7 +415,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
     }
     __syncthreads();
 
-    // Row loads of one neighbour-slot chunk (a ping-pong group): a thread owns
+    // Row loads of one neighbour-slot chunk (a message group): a thread owns
     // one 8-feature column chunk (tid % 16) of six slot rows: the slot table
     // row (W1b h_E + W1d h_enc of the neighbour, 16-bit) and, for a decoded
     // neighbour at layers 1 and 2, its correction row W1d (h_j - h_enc_j).
@@ -546,15 +546,14 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         }
       }
       // ---- messages: gather + GELU -> W2 MMA -> GELU + slot sum ------------
-      // Two ping-pong groups of 8 warps; group g takes chunks g, g+2, ... and
-      // owns operand buffer g and D2 buffer g.  Per chunk a group builds the
+      // kGroups groups; group g takes chunks g, g + kGroups, ... and owns
+      // operand buffer g and D2 buffer g.  Per chunk a group builds the
       // operand from rows already in registers, one elected thread issues
       // the MMA, the group issues the row loads of its next chunk (chunk g
       // of the next layer after its last one; they stay in flight through
       // the W3 / FFN phases), then waits for D2 and sums GELU(D2 + b2) over
-      // the slots.  While one group waits on its MMA or sums, the other
-      // builds, so the two halves of the work overlap without handing
-      // buffers across groups.
+      // the slots.  While one group waits on its MMA or sums, the others
+      // build, so the work overlaps without handing buffers across groups.
       {
         // The PE rows (W1b h_E: K contiguous rows per sequence) of the next
         // message phase -- layer l+1 here, or layer 0 at the next position --
