@@ -485,12 +485,15 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     {
       float v[32];
       tmem_ld32(tm + lane_base + 128u + (uint32_t)c0, v);
+      const float4* b12 = reinterpret_cast<const float4*>(p.b12 + c0);   // warp-uniform
       uint32_t pk[16];
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const float2 y = gelu_tc_x2(make_float2(v[2 * q] + p.b12[c0 + 2 * q],
-                                                v[2 * q + 1] + p.b12[c0 + 2 * q + 1]));
-        pk[q] = pack_h2(y.x, y.y);
+      for (int q = 0; q < 8; ++q) {
+        const float4 b = b12[q];
+        const float2 y0 = gelu_tc_x2(make_float2(v[4 * q] + b.x, v[4 * q + 1] + b.y));
+        const float2 y1 = gelu_tc_x2(make_float2(v[4 * q + 2] + b.z, v[4 * q + 3] + b.w));
+        pk[2 * q] = pack_h2(y0.x, y0.y);
+        pk[2 * q + 1] = pack_h2(y1.x, y1.y);
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u)
@@ -531,6 +534,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     {
       float x[32];
       tmem_ld32(tm + lane_base + (uint32_t)c0, x);
+      const float2* b13 = reinterpret_cast<const float2*>(p.b13 + c0);   // warp-uniform
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const uint4 hv = hres[u], lv = lres[u];
@@ -539,16 +543,19 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         for (int i = 0; i < 4; ++i) {
           const float2 h2 = __half22float2(*reinterpret_cast<const __half2*>(&hw[i]));
           const float2 l2 = __half22float2(*reinterpret_cast<const __half2*>(&lw[i]));
+          const float2 b = b13[4 * u + i];
           const int c = 8 * u + 2 * i;
-          x[c] += (h2.x + l2.x) + p.b13[c0 + c];
-          x[c + 1] += (h2.y + l2.y) + p.b13[c0 + c + 1];
+          x[c] += (h2.x + l2.x) + b.x;
+          x[c + 1] += (h2.y + l2.y) + b.y;
         }
       }
       float sum = 0.0f;
 #pragma unroll
       for (int i = 0; i < 32; ++i) sum += x[i];
+      // a row's four 32-column parts belong to warps quad, quad+4, quad+8,
+      // quad+12: a named barrier over those four suffices
       red[0][cg][row] = sum;
-      __syncthreads();
+      named_bar_sync(1 + quad, 128);
       const float mean =
           (red[0][0][row] + red[0][1][row] + red[0][2][row] + red[0][3][row]) * (1.0f / 128.0f);
       float sq = 0.0f;
@@ -558,13 +565,21 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         sq += x[i] * x[i];
       }
       red[1][cg][row] = sq;
-      __syncthreads();
+      named_bar_sync(1 + quad, 128);
       const float var =
           (red[1][0][row] + red[1][1][row] + red[1][2][row] + red[1][3][row]) * (1.0f / 128.0f);
       const float inv = 1.0f / sqrtf(var + kLnEps);
       if (rj >= 0) {
+        const float4* gw = reinterpret_cast<const float4*>(p.n3w + c0);   // warp-uniform
+        const float4* gb = reinterpret_cast<const float4*>(p.n3b + c0);
 #pragma unroll
-        for (int q = 0; q < 32; ++q) x[q] = x[q] * inv * p.n3w[c0 + q] + p.n3b[c0 + q];
+        for (int q = 0; q < 8; ++q) {
+          const float4 g = gw[q], b = gb[q];
+          x[4 * q] = x[4 * q] * inv * g.x + b.x;
+          x[4 * q + 1] = x[4 * q + 1] * inv * g.y + b.y;
+          x[4 * q + 2] = x[4 * q + 2] * inv * g.z + b.z;
+          x[4 * q + 3] = x[4 * q + 3] * inv * g.w + b.w;
+        }
         store_hi_lo(p.h_e_out + s * kH + c0, p.h_e_lo + s * kH + c0, x);
       }
     }
