@@ -863,9 +863,11 @@ def run_small(args):
 
 def run_profile_case(args):
     """One untimed call on a small case for ncu captures: ``design`` runs
-    N backbones x L=256 x 32 sequences (T=0.1), ``score`` the teacher-forced
-    pass over N backbones x L=384 x 16 random sequences (the config-2 and
-    config-4 shapes with N proteins, default 16)."""
+    N backbones x L=256 x S sequences (T=0.1; S = 32 by default, 128 gives
+    the config-2 occupancy of 14 sequences per decode CTA on 16 backbones),
+    ``score`` the teacher-forced pass over N backbones x L=384 x 16 random
+    sequences (the config-2 and config-4 shapes with N proteins, default
+    16)."""
     from hikoboshi_b200 import DesignEngine, synthetic_backbone
     n = args.profile_proteins
     eng = DesignEngine(WEIGHTS, device=0, precision=args.precision)
@@ -875,9 +877,9 @@ def run_profile_case(args):
         case = f"{n} x L=384 x 16 teacher-forced"
     else:
         bb = [synthetic_backbone(i, L_RES) for i in range(n)]
-        eng.design([b[0] for b in bb], [b[1] for b in bb], num_seqs=N_SEQ, seeds=list(range(n)),
-                   temperatures=TEMP, keep_log_probs=True)
-        case = f"{n} x L=256 x 32 design"
+        eng.design([b[0] for b in bb], [b[1] for b in bb], num_seqs=args.profile_seqs,
+                   seeds=list(range(n)), temperatures=TEMP, keep_log_probs=True)
+        case = f"{n} x L=256 x {args.profile_seqs} design"
     print(json.dumps({"profile_case": case, "precision": args.precision, **eng.last_timings()}))
     eng.close()
     return 0
@@ -899,6 +901,7 @@ def main():
                     help="one untimed call on a small case (for ncu captures)")
     ap.add_argument("--profile-workload", choices=["design", "score"], default="design")
     ap.add_argument("--profile-proteins", type=int, default=16)
+    ap.add_argument("--profile-seqs", type=int, default=32)
     args = ap.parse_args()
     if args.profile_case:
         return run_profile_case(args)
