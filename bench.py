@@ -12,6 +12,9 @@ decode of all 2,048 sequences (524,288 designed residues per GPU).
   write) before each step.
 * ``e2e``    -- the host API (hkb_mpnn_design): pinned coords/atom-sources
   uploaded and tokens + log-probs + scores read back every step; wall clock.
+  The log-probs buffer is pinned, so the decode kernel writes the rows into it
+  as it samples them (the same bytes cross the bus, during the kernel instead
+  of in a copy after it).
 * ``roofline`` -- the autoregressive decode kernel (the dominant kernel):
   algorithmic FLOPs per launch (29,103,360 per designed residue, the reference
   formulation) over its CUDA-event duration, against the measured burst 16-bit

@@ -1019,10 +1019,11 @@ hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   int* d_g0 = ws.get_as<int>("a.gseq", (size_t)ng * G);
   int* d_gc = ws.get_as<int>("a.gc", ng);
   int* pos = ws.get_as<int>("a.pos", hb.Q);
+  float* lp_tok = ws.get_as<float>("a.lptok", hb.Q);
   uint16_t* PV = ws.get_as<uint16_t>("b.PV", 2 * hb.Q * kH);
   uint64_t* seeds = ws.get_as<uint64_t>("a.seed", hb.NS);
   float* temps = ws.get_as<float>("a.temp", hb.NS);
-  if (!d_g0 || !d_gc || !pos || !PV || !seeds || !temps)
+  if (!d_g0 || !d_gc || !pos || !lp_tok || !PV || !seeds || !temps)
     return {HKB_UNAVAILABLE, "device allocation failed"};
   HKB_CUDA(cudaMemcpyAsync(d_g0, gseq.data(), sizeof(int) * gseq.size(), cudaMemcpyHostToDevice,
                            st));
@@ -1036,6 +1037,7 @@ hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   a.pos = pos;
   a.tokens = o.tokens;
   a.log_probs = o.log_probs;
+  a.lp_tok = lp_tok;
   a.PV = PV;
   a.seq_seed = seeds;
   a.seq_temp = temps;
@@ -1047,7 +1049,9 @@ hkb_status decode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
     --e->stall_check_calls;
   }
   launch_ar_decode_tc(st, db.bv, e->wbf, tb, a, f16, e->d_err);
-  launch_scores(st, db.bv, o.tokens, o.log_probs, eo.mask, o.scores);
+  // the scores read the sampled tokens' log-probs from lp_tok, never the
+  // [Q,21] rows, which may live in mapped host memory
+  launch_scores(st, db.bv, o.tokens, o.log_probs, eo.mask, o.scores, lp_tok);
   e->launches += 2;
   return kOk;
 }
@@ -1593,16 +1597,31 @@ hkb_status hkb_mpnn_design(hkb_engine* e, const hkb_design_batch* batch,
   }
   DeviceDesignOut o;
   o.tokens = e->ws.get_as<int>("o.tokens", Q);
-  o.log_probs = e->ws.get_as<float>("o.lp", Q * kV);
   o.orders = e->ws.get_as<int>("o.orders", Q);
   o.scores = e->ws.get_as<float>("o.scores", NS);
+  // A page-locked, mapped log_probs buffer (cudaHostAlloc / cudaHostRegister)
+  // is written by the tensor-core decode kernel directly, so its 84 bytes per
+  // designed residue cross the bus while the kernel runs instead of in a copy
+  // after it; anything else gets a device buffer and a copy.
+  bool lp_direct = false;
+  if (out->log_probs && e->precision != HKB_PRECISION_FP32) {
+    cudaPointerAttributes pa{};
+    if (cudaPointerGetAttributes(&pa, out->log_probs) == cudaSuccess &&
+        pa.type == cudaMemoryTypeHost && pa.devicePointer != nullptr) {
+      o.log_probs = static_cast<float*>(pa.devicePointer);
+      lp_direct = true;
+    } else {
+      (void)cudaGetLastError();   // an unregistered pointer is not an error here
+    }
+  }
+  if (!lp_direct) o.log_probs = e->ws.get_as<float>("o.lp", Q * kV);
   if (!o.tokens || !o.log_probs || !o.orders || !o.scores)
     return {HKB_UNAVAILABLE, "device allocation failed"};
   HostBatch hb;
   hkb_status s = design_common(e, batch, batch->atom_sources, d_coords, d_src, &hb, o);
   if (s.code != HKB_OK) return s;
   HKB_CUDA(cudaMemcpyAsync(out->tokens, o.tokens, sizeof(int) * Q, cudaMemcpyDeviceToHost, st));
-  if (out->log_probs)
+  if (out->log_probs && !lp_direct)
     HKB_CUDA(cudaMemcpyAsync(out->log_probs, o.log_probs, sizeof(float) * Q * kV,
                              cudaMemcpyDeviceToHost, st));
   if (out->scores)

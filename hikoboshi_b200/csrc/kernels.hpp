@@ -221,7 +221,8 @@ struct ArBf16Args {
   const int* orders;
   int* pos;
   int* tokens;
-  float* log_probs;
+  float* log_probs;          // [Q,21]: device memory or mapped pinned host memory
+  float* lp_tok;             // [Q] log-prob of the sampled token (0 where masked)
   uint16_t* PV;              // 16-bit [2,Q,128] (rows written before they are read)
   const uint64_t* seq_seed;
   const float* seq_temp;
@@ -395,7 +396,10 @@ struct OrderArgs {
 };
 void launch_decode_orders(cudaStream_t st, const OrderArgs& a);
 
+// Mean NLL per sequence over unmasked residues.  With lp_tok ([Q], the
+// sampled token's log-prob per row) the [Q,21] log_probs are not read.
 void launch_scores(cudaStream_t st, const BatchView& bv, const int* tokens,
-                   const float* log_probs, const float* mask, float* scores);
+                   const float* log_probs, const float* mask, float* scores,
+                   const float* lp_tok = nullptr);
 
 }  // namespace hkb

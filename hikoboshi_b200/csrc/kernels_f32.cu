@@ -608,7 +608,8 @@ __global__ void log_softmax_rows_kernel(int64_t rows, const float* __restrict__ 
 __global__ void scores_kernel(BatchView bv, const int* __restrict__ tokens,
                               const float* __restrict__ lp,
                               const float* __restrict__ mask,
-                              float* __restrict__ scores) {
+                              float* __restrict__ scores,
+                              const float* __restrict__ lp_tok) {
   const int sq = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (sq >= bv.num_sequences) return;
@@ -621,7 +622,7 @@ __global__ void scores_kernel(BatchView bv, const int* __restrict__ tokens,
     const float m = mask[off + t];
     const int tok = tokens[q0 + t];
     if (m == 0.0f || tok < 0 || tok >= kV) continue;
-    loss -= (double)lp[(q0 + t) * kV + tok];
+    loss -= (double)(lp_tok ? lp_tok[q0 + t] : lp[(q0 + t) * kV + tok]);
     cnt += (double)m;
   }
 #pragma unroll
@@ -1077,10 +1078,11 @@ void launch_log_softmax_rows(cudaStream_t st, int64_t rows, const float* logits,
 }
 
 void launch_scores(cudaStream_t st, const BatchView& bv, const int* tokens,
-                   const float* log_probs, const float* mask, float* scores) {
+                   const float* log_probs, const float* mask, float* scores,
+                   const float* lp_tok) {
   if (bv.num_sequences <= 0) return;
   scores_kernel<<<grid_rows(bv.num_sequences, 8), 256, 0, st>>>(bv, tokens, log_probs,
-                                                               mask, scores);
+                                                               mask, scores, lp_tok);
 }
 
 void launch_ar_decode_f32(cudaStream_t st, const BatchView& bv, const F32Weights& w,

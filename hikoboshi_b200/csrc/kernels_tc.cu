@@ -875,6 +875,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       float* lp = a.log_probs + q * kV;
       const bool in_vocab = lane < kV;
       int tok = kV - 1;
+      float lpv = 0.0f;   // this lane's log-prob (0 for a masked residue)
       if (M.m[s] == 0.0f) {
         if (in_vocab) lp[lane] = 0.0f;
       } else {
@@ -886,7 +887,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         const float e = in_vocab ? expf(z - mx) : 0.0f;
         const float sum = warp_sum(e);
         const float ls = logf(sum), inv = 1.0f / sum;
-        if (in_vocab) lp[lane] = (z - mx) - ls;
+        lpv = in_vocab ? (z - mx) - ls : 0.0f;
+        if (in_vocab) lp[lane] = lpv;
         if (greedy) {
           const unsigned top = __ballot_sync(0xffffffffu, in_vocab && z == mx);
           tok = top ? __ffs(top) - 1 : 0;
@@ -908,8 +910,10 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           if (hit) tok = __ffs(hit) - 1;
         }
       }
+      const float lpt = __shfl_sync(0xffffffffu, lpv, tok);
       if (lane == 0) {
         a.tokens[q] = tok;
+        a.lp_tok[q] = lpt;
         M.tok_cur[s] = tok;
       }
     }

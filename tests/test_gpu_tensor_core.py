@@ -272,3 +272,48 @@ def test_sharded_design_single_gpu_matches_engine(engine_f16):
         assert (got.tokens[b] == want.tokens[b]).all(), b
         assert (got.orders[b] == want.orders[b]).all(), b
         assert (got.scores[b].view(np.uint32) == want.scores[b].view(np.uint32)).all(), b
+
+
+def test_pinned_log_probs_written_in_place(engine_f16):
+    """A page-locked log_probs buffer is written by the decode kernel directly
+    (no copy after it); tokens, orders, log-probs and scores equal the
+    pageable-buffer call's bit for bit."""
+    import ctypes
+    import torch
+    from hikoboshi_b200 import _lib
+    Ls, Ss, temps, modes, coords, sources = _batch()
+    modes_a = np.array([0 if m == "random" else 1 for m in modes], np.int32)
+    L = np.array(Ls, np.int32)
+    S = np.array(Ss, np.int32)
+    seeds = np.arange(len(Ls), dtype=np.uint64) * np.uint64(7) + np.uint64(5)
+    T = np.array(temps, np.float32)
+    cc = np.ascontiguousarray(np.concatenate([c.reshape(-1, 5, 3) for c in coords]), np.float32)
+    ss = np.ascontiguousarray(np.concatenate([s.reshape(-1, 5) for s in sources]), np.uint8)
+    Q = int((S.astype(np.int64) * L).sum())
+    NS = int(S.sum())
+    P = ctypes.POINTER
+    batch = _lib.DesignBatch(len(Ls), L.ctypes.data_as(P(ctypes.c_int32)),
+                             cc.ctypes.data_as(ctypes.c_void_p), ss.ctypes.data_as(ctypes.c_void_p),
+                             S.ctypes.data_as(P(ctypes.c_int32)),
+                             seeds.ctypes.data_as(P(ctypes.c_uint64)),
+                             T.ctypes.data_as(P(ctypes.c_float)),
+                             modes_a.ctypes.data_as(P(ctypes.c_int32)), None)
+
+    def call(lp_ptr):
+        tok = np.zeros(Q, np.int32)
+        order = np.zeros(Q, np.int32)
+        sc = np.zeros(NS, np.float32)
+        out = _lib.DesignOut(tok.ctypes.data_as(ctypes.c_void_p), lp_ptr,
+                             order.ctypes.data_as(ctypes.c_void_p),
+                             sc.ctypes.data_as(ctypes.c_void_p))
+        _lib.check(engine_f16._lib.hkb_mpnn_design(engine_f16._h, ctypes.byref(batch),
+                                                   ctypes.byref(out)))
+        return tok, order, sc
+
+    lp_page = np.full((Q, 21), np.nan, np.float32)
+    tok_a, ord_a, sc_a = call(lp_page.ctypes.data_as(ctypes.c_void_p))
+    lp_pin = torch.full((Q, 21), float("nan"), dtype=torch.float32).pin_memory()
+    tok_b, ord_b, sc_b = call(ctypes.c_void_p(lp_pin.data_ptr()))
+    assert (tok_a == tok_b).all() and (ord_a == ord_b).all()
+    assert np.array_equal(lp_page, lp_pin.numpy())
+    assert np.array_equal(sc_a, sc_b)
