@@ -510,19 +510,52 @@ def run_config4(args):
     barrier()
     clocks = ClockSampler(local)
     clocks.start()
-    dev_ms, tf_ms, wall_ms, launches = [], [], [], 0
+    dev_ms, tf_ms, launches = [], [], 0
     for _ in range(args.steps):
         flush.zero_()
         torch.cuda.synchronize(dev)
-        t0 = time.perf_counter()
         step()
-        wall_ms.append((time.perf_counter() - t0) * 1000)
         tm = eng.last_timings()
         dev_ms.append(tm["total_ms"])
         tf_ms.append(tm["decode_ms"])
         launches += eng.last_launch_count()
     barrier()
     clk = clocks.stop()
+
+    # end-to-end through the host API (hkb_mpnn_score) with pinned host
+    # buffers: coordinates, atom sources and tokens uploaded, log-probs,
+    # orders and scores read back every call
+    import hikoboshi_b200._lib as hl
+    P = ctypes.POINTER
+    L = np.full(C4_PROT, C4_L, np.int32)
+    S = np.full(C4_PROT, C4_SEQ, np.int32)
+    seeds = np.full(C4_PROT, 3, np.uint64)
+    pin_c = torch.from_numpy(np.ascontiguousarray(np.concatenate(cs), np.float32)).pin_memory()
+    pin_s = torch.from_numpy(np.ascontiguousarray(np.concatenate(ss), np.uint8)).pin_memory()
+    pin_t = torch.from_numpy(np.ascontiguousarray(np.concatenate([t.reshape(-1) for t in toks]),
+                                                  np.int32)).pin_memory()
+    h_lp = torch.empty(Q * 21, dtype=torch.float32).pin_memory()
+    h_ord = torch.empty(Q, dtype=torch.int32).pin_memory()
+    h_sc = torch.empty(C4_PROT * C4_SEQ, dtype=torch.float32).pin_memory()
+    sb = hl.ScoreBatch(C4_PROT, L.ctypes.data_as(P(ctypes.c_int32)),
+                       ctypes.c_void_p(pin_c.data_ptr()), ctypes.c_void_p(pin_s.data_ptr()),
+                       S.ctypes.data_as(P(ctypes.c_int32)),
+                       ctypes.cast(ctypes.c_void_p(pin_t.data_ptr()), P(ctypes.c_int32)),
+                       None, seeds.ctypes.data_as(P(ctypes.c_uint64)))
+    so = hl.ScoreOut(ctypes.c_void_p(h_lp.data_ptr()), ctypes.c_void_p(h_ord.data_ptr()),
+                     ctypes.c_void_p(h_sc.data_ptr()))
+
+    def host_step():
+        hl.check(hl.load().hkb_mpnn_score(eng._h, ctypes.byref(sb), ctypes.byref(so)))
+
+    host_step()
+    barrier()
+    wall_ms = []
+    for _ in range(max(1, min(args.steps, 5))):
+        t0 = time.perf_counter()
+        host_step()
+        wall_ms.append((time.perf_counter() - t0) * 1000)
+    barrier()
     stats = torch.tensor([np.mean(dev_ms), np.mean(tf_ms), np.mean(wall_ms)], dtype=torch.float64,
                          device=dev)
     if world > 1:
@@ -543,8 +576,8 @@ def run_config4(args):
                        "precision": args.precision,
                        "l2": "flushed before every step (512 MiB write, outside the timing)",
                        "timing": "value: device events around the pipeline (encoder, tables, "
-                                 "teacher-forced layers); e2e: the host call with uploads and "
-                                 "log-prob read-back"},
+                                 "teacher-forced layers); e2e: the host call (hkb_mpnn_score) "
+                                 "from pinned buffers with uploads and log-prob read-back"},
             "tf_ms": t_ms,
             "roofline": {"bound": "tensor", "kernel": "teacher-forced layers (tf_slot_tc + tf_node_tc)",
                          "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
