@@ -126,7 +126,11 @@ void hkb_mpnn_destroy(hkb_engine* engine);
  * (cpp/algorithms/inverse_fold.cpp:221-356) around
  * modules::mpnn::proteinmpnn_inverse_fold_scalar
  * (cpp/modules/mpnn/inverse_fold_scalar.cpp:954-1000), for many proteins at
- * once.  Validation mirrors algorithms/inverse_fold.cpp:232-261. */
+ * once.  Validation mirrors algorithms/inverse_fold.cpp:232-261.
+ * A log_probs buffer in page-locked, mapped host memory (cudaHostAlloc,
+ * cudaHostRegister) is written by the 16-bit engines' decode kernel directly
+ * as it samples, with no copy after the kernel; any other buffer receives a
+ * copy.  The results are identical either way. */
 hkb_status hkb_mpnn_design(hkb_engine* engine, const hkb_design_batch* batch,
                            hkb_design_out* out);
 
