@@ -1600,14 +1600,15 @@ hkb_status hkb_mpnn_design(hkb_engine* e, const hkb_design_batch* batch,
   o.orders = e->ws.get_as<int>("o.orders", Q);
   o.scores = e->ws.get_as<float>("o.scores", NS);
   // A page-locked, mapped log_probs buffer (cudaHostAlloc / cudaHostRegister)
-  // is written by the tensor-core decode kernel directly, so its 84 bytes per
-  // designed residue cross the bus while the kernel runs instead of in a copy
-  // after it; anything else gets a device buffer and a copy.
+  // registered against this engine's device is written by the tensor-core
+  // decode kernel directly, so its 84 bytes per designed residue cross the
+  // bus while the kernel runs instead of in a copy after it; anything else
+  // gets a device buffer and a copy.
   bool lp_direct = false;
   if (out->log_probs && e->precision != HKB_PRECISION_FP32) {
     cudaPointerAttributes pa{};
     if (cudaPointerGetAttributes(&pa, out->log_probs) == cudaSuccess &&
-        pa.type == cudaMemoryTypeHost && pa.devicePointer != nullptr) {
+        pa.type == cudaMemoryTypeHost && pa.devicePointer != nullptr && pa.device == e->device) {
       o.log_probs = static_cast<float*>(pa.devicePointer);
       lp_direct = true;
     } else {
