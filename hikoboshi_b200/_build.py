@@ -22,8 +22,8 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU_SOURCES = ["kernels_f32.cu", "kernels_tc.cu", "enc_tc.cu", "tf_tc.cu", "orders.cu", "engine.cu",
-              "noalloc.cu"]
+CU_SOURCES = ["kernels_f32.cu", "kernels_tc.cu", "enc_tc.cu", "tf_tc.cu", "gemm_tc.cu", "orders.cu",
+              "engine.cu", "noalloc.cu"]
 CPP_SOURCES = ["host_order.cpp", "host_synth.cpp", "safetensors.cpp", "structure_io.cpp",
                "host_io.cpp"]
 

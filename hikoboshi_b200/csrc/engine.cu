@@ -464,8 +464,8 @@ void append_gemm_image(std::vector<uint16_t>& img, const float* W, int ld, int r
     }
 }
 
-// The 16-bit GEMM operands of the fused tensor-core encoder kernels and the
-// decoder's PE tables, by name (the node-side GEMMs run in fp32).
+// The 16-bit GEMM operands of the fused tensor-core encoder kernels, the
+// decoder's slot tables and the node-side GEMMs (gemm_tc3), by name.
 bool build_gemm_images(const std::map<std::string, TensorView>& t, std::vector<uint16_t>* img,
                        std::map<std::string, size_t>* at) {
   auto get = [&](const std::string& n) -> const float* {
@@ -508,6 +508,44 @@ bool build_gemm_images(const std::map<std::string, TensorView>& t, std::vector<u
     if (!W1) return false;
     mark(q + "W1b");
     append_gemm_image(*img, W1, 512, 0, 128, 128, 128);
+  }
+  // Node-side GEMMs (gemm_tc3): value (".hi") and remainder (".lo") images,
+  // one 128-row block per 128 output columns, blocks in output order.
+  for (int lo = 0; lo < 2; ++lo) {
+    const char* sfx = lo ? ".lo" : ".hi";
+    for (int l = 0; l < 3; ++l) {
+      const std::string p = "encoder_layers." + std::to_string(l) + ".";
+      const std::string q = "enc" + std::to_string(l) + ".";
+      const float* W1 = get(p + "W1.weight");
+      const float* W11 = get(p + "W11.weight");
+      const float* W3 = get(p + "W3.weight");
+      const float* Wi = get(p + "dense.W_in.weight");
+      const float* Wo = get(p + "dense.W_out.weight");
+      if (!W1 || !W11 || !W3 || !Wi || !Wo) return false;
+      mark(q + "nW1ac" + sfx);   // [W1a | W1c]: the h_i and h_j input blocks
+      append_gemm_image(*img, W1, 384, 0, 128, 0, 128, lo);
+      append_gemm_image(*img, W1, 384, 0, 128, 256, 128, lo);
+      mark(q + "nW11ac" + sfx);
+      append_gemm_image(*img, W11, 384, 0, 128, 0, 128, lo);
+      append_gemm_image(*img, W11, 384, 0, 128, 256, 128, lo);
+      mark(q + "nW3" + sfx);
+      append_gemm_image(*img, W3, 128, 0, 128, 0, 128, lo);
+      mark(q + "nWin" + sfx);
+      for (int nb = 0; nb < 4; ++nb) append_gemm_image(*img, Wi, 128, 128 * nb, 128, 0, 128, lo);
+      mark(q + "nWout" + sfx);
+      append_gemm_image(*img, Wo, 512, 0, 128, 0, 512, lo);
+    }
+    for (int l = 0; l < 3; ++l) {
+      const std::string p = "decoder_layers." + std::to_string(l) + ".";
+      const std::string q = "dec" + std::to_string(l) + ".";
+      const float* W1 = get(p + "W1.weight");
+      mark(q + "nW1d" + sfx);    // the h_j input block
+      append_gemm_image(*img, W1, 512, 0, 128, 384, 128, lo);
+      if (l == 0) {
+        mark(q + "nW1a" + sfx);  // the h_t input block
+        append_gemm_image(*img, W1, 512, 0, 128, 0, 128, lo);
+      }
+    }
   }
   return true;
 }
@@ -784,12 +822,13 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
       !T3 || !h1 || !F || !Y)
     return {HKB_UNAVAILABLE, "device allocation failed"};
   const BatchView& bv = db.bv;
-  // Node-side GEMMs (M = R residue rows) in fp32 on the packed fp32 pipe:
-  // they are a small share of the encoder's work, and keeping them at fp32
-  // removes the largest 16-bit error source of the encoder.
-  auto lin = [&](int N, int K, const float* A, int lda, const float* WT, const float* bias,
+  // Node-side GEMMs (M = R residue rows) on tcgen05 with both operands as
+  // fp16 value + remainder (about 22 significant bits each, close to fp32:
+  // their 16-bit rounding would be the largest error source of the encoder).
+  auto lin = [&](int N, int K, const float* A, int lda, const std::string& W, const float* bias,
                  int act, float* C, int ldc) {
-    gemm_f32(st, R, N, K, A, lda, WT, N, bias, act, C, ldc);
+    gemm_tc3(st, R, N, K, A, lda, e->gemm_img.at(W + ".hi"), e->gemm_img.at(W + ".lo"), bias,
+             act, C, ldc, false, e->d_err);
     e->launches += 1;
   };
   launch_knn(st, bv, db.coords, db.sources, eo->e_idx, eo->d2, eo->mask, e->d_err, hb.max_len);
@@ -816,7 +855,7 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
     const auto& E = w.enc[l];
     const std::string q = "enc" + std::to_string(l) + ".";
     // node messages: one fused pass over h_E (W1b, gathers, GELU, W2, GELU, slot sum)
-    lin(256, kH, eo->h_v, kH, E.W1acT, E.b1ac, 0, NAC, 256);
+    lin(256, kH, eo->h_v, kH, q + "nW1ac", E.b1ac, 0, NAC, 256);
     EncNodeTcArgs na;
     na.bv = bv;
     na.h_e = eo->h_e16;
@@ -832,13 +871,13 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
     na.cnt = cnt;
     na.err = e->d_err;
     launch_enc_node_tc(st, na, e->num_sms);
-    lin(kH, kH, Sv, kH, E.W3T, nullptr, 0, T3, kH);
+    lin(kH, kH, Sv, kH, q + "nW3", nullptr, 0, T3, kH);
     launch_enc_node_update(st, bv, T3, cnt, E.b3, eo->h_v, E.n1w, E.n1b, h1);
-    lin(kFfn, kH, h1, kH, E.WinT, E.bin, 1, F, kFfn);
-    lin(kH, kFfn, F, kFfn, E.WoutT, nullptr, 0, Y, kH);
+    lin(kFfn, kH, h1, kH, q + "nWin", E.bin, 1, F, kFfn);
+    lin(kH, kFfn, F, kFfn, q + "nWout", nullptr, 0, Y, kH);
     launch_ln_rows(st, R, h1, Y, E.bout, E.n2w, E.n2b, eo->mask, nullptr, eo->h_v);
     // edge update: one fused pass (W11b, gathers, GELU, W12, GELU, W13, LN3)
-    lin(256, kH, eo->h_v, kH, E.W11acT, E.b11ac, 0, NAC, 256);
+    lin(256, kH, eo->h_v, kH, q + "nW11ac", E.b11ac, 0, NAC, 256);
     EncEdgeTcArgs ea;
     ea.bv = bv;
     ea.h_e = eo->h_e16;
@@ -884,8 +923,10 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const BatchView
     ta.W[l] = e->gemm_img.at(q + "W1b");
     ta.PVenc[l] = pv;
     ta.out[l] = pe;
-    // W1d h_enc per residue, fp32 products rounded once to the 16-bit table
-    gemm_f32x2(st, R, kH, kH, eo.h_v, kH, e->w32.dec[l].W1dT, kH, nullptr, 0, pv, kH, true);
+    // W1d h_enc per residue (value + remainder products, about fp32
+    // precision) rounded once to the 16-bit table
+    gemm_tc3(st, R, kH, kH, eo.h_v, kH, e->gemm_img.at(q + "nW1d.hi"),
+             e->gemm_img.at(q + "nW1d.lo"), nullptr, 0, pv, kH, true, e->d_err);
     tb->PE[l] = pe;
     tb->PVenc[l] = pv;
   }
@@ -893,7 +934,8 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const BatchView
   if (with_pe) launch_dec_tables_tc(st, ta, e->num_sms);
   float* a0 = ws.get_as<float>("d.Aenc0", R * kH);
   if (!a0) return {HKB_UNAVAILABLE, "device allocation failed"};
-  gemm_f32(st, R, kH, kH, eo.h_v, kH, e->w32.dec[0].W1aT, kH, e->w32.dec[0].b1, 0, a0, kH);
+  gemm_tc3(st, R, kH, kH, eo.h_v, kH, e->gemm_img.at("dec0.nW1a.hi"),
+           e->gemm_img.at("dec0.nW1a.lo"), e->w32.dec[0].b1, 0, a0, kH, false, e->d_err);
   tb->Aenc0 = a0;
   tb->h_enc = eo.h_v;
   e->launches += 5;

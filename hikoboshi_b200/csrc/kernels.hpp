@@ -88,6 +88,13 @@ bool gemm_f32x2_fits(int N, int K, const void* A, int lda, const void* B, int ld
 void gemm_f32x2(cudaStream_t st, int64_t M, int N, int K, const float* A, int lda,
                 const float* B, int ldb, const float* bias, int act, void* C, int ldc,
                 bool out_f16);
+// The same contraction on tcgen05 with both operands applied as fp16 value +
+// fp16 remainder (three products): W given as value and remainder images
+// (append_gemm_image layout, one 128-row block per 128 output columns), N a
+// multiple of 128, K of 64, lda of 4; act 0 none, 1 GELU (fp32 output only).
+void gemm_tc3(cudaStream_t st, int64_t M, int N, int K, const float* A, int lda,
+              const unsigned char* Whi, const unsigned char* Wlo, const float* bias, int act,
+              void* C, int ldc, bool out_f16, unsigned int* err);
 
 // Largest protein one call accepts (kNN keeps one 8-byte key per candidate
 // in shared memory and ranks every candidate against every other).

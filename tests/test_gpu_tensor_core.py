@@ -317,3 +317,41 @@ def test_pinned_log_probs_written_in_place(engine_f16):
     assert (tok_a == tok_b).all() and (ord_a == ord_b).all()
     assert np.array_equal(lp_page, lp_pin.numpy())
     assert np.array_equal(sc_a, sc_b)
+
+
+def test_two_engines_from_two_threads(weights_path):
+    """Two engines driven from two host threads at once (one engine per
+    thread, the supported pattern) give exactly the results each gives alone:
+    per-engine streams and workspaces, and the once-per-(device, kernel)
+    shared-memory opt-in is thread-safe."""
+    import threading
+    from hikoboshi_b200 import DesignEngine, synthetic_backbone
+    bb = [synthetic_backbone(900 + i, L) for i, L in enumerate([64, 97, 130])]
+    cs, ss = [b[0] for b in bb], [b[1] for b in bb]
+    engines = [DesignEngine(weights_path, device=0, precision=p) for p in ("f16", "bf16")]
+    try:
+        alone = [e.design(cs, ss, 6, seeds=[1, 2, 3], temperatures=0.1) for e in engines]
+        got = [None, None]
+        errors = []
+
+        def run(i):
+            try:
+                for _ in range(3):
+                    got[i] = engines[i].design(cs, ss, 6, seeds=[1, 2, 3], temperatures=0.1)
+            except Exception as exc:   # surfaced below
+                errors.append(exc)
+
+        threads = [threading.Thread(target=run, args=(i,)) for i in range(2)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join(timeout=300)
+        assert not errors, errors
+        for i in range(2):
+            for b in range(3):
+                assert np.array_equal(alone[i].tokens[b], got[i].tokens[b])
+                assert np.array_equal(alone[i].log_probs[b], got[i].log_probs[b])
+                assert np.array_equal(alone[i].scores[b], got[i].scores[b])
+    finally:
+        for e in engines:
+            e.close()
