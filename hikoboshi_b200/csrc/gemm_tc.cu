@@ -12,12 +12,12 @@
 // One CTA per (128-row tile, 128-column block): the weights are the A operand
 // (M = 128 output features on TMEM lanes), the activation rows the B operand
 // (N = 128 rows on TMEM columns).  K advances one 64-column atom at a time
-// through two shared-memory stages: thread 0 loads the weight atoms (value and
+// through a shared-memory stage: thread 0 loads the weight atoms (value and
 // remainder images prepared at engine creation) by bulk copy, the 512 threads
 // load the fp32 activation atom and split it into the value and remainder
 // operand atoms, and thread 0 issues the three K = 64 products and commits
-// them to the stage's mbarrier; the next atom's activations load while the
-// current products run.  The epilogue adds the bias, applies the activation
+// them to the stage's mbarrier.  Two CTAs share an SM, so one CTA's loads and
+// epilogue overlap the other's products.  The epilogue adds the bias, applies the activation
 // (the reference's erf GELU) and stores rows feature-contiguous (a warp writes
 // 32 consecutive columns of one row).  Every wait is bounded.
 #include <cuda_fp16.h>
@@ -31,10 +31,17 @@ namespace {
 
 using namespace tc;
 
+// One stage (64 KiB) lets two CTAs share an SM, which measured faster than
+// two stages (the activation load then overlaps the other CTA's products and
+// epilogue instead of this CTA's own).
+#ifndef HKB_GT_STAGES
+#define HKB_GT_STAGES 1
+#endif
 constexpr int kGtThreads = 512;
+constexpr int kGtStages = HKB_GT_STAGES;          // shared-memory stages
 constexpr uint32_t kGtAtom = 128 * 128;           // 128 rows x 64 fp16 (SW128)
 constexpr uint32_t kGtStage = 4 * kGtAtom;        // W hi, W lo, A hi, A lo
-constexpr uint32_t kGtSmem = 2 * kGtStage + 1024;
+constexpr uint32_t kGtSmem = kGtStages * kGtStage + 1024;
 
 __device__ __forceinline__ uint32_t idesc_h16(int M, int N) {
   return idesc_bf16(M, N) & ~((7u << 7) | (7u << 10));
@@ -62,7 +69,7 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t&
 }
 
 template <int ACT, bool OUT16>
-__global__ void __launch_bounds__(kGtThreads, 1) gemm_tc3_kernel(
+__global__ void __launch_bounds__(kGtThreads, 3 - kGtStages) gemm_tc3_kernel(
     int64_t M, int K, const float* __restrict__ A, int lda,
     const unsigned char* __restrict__ Whi, const unsigned char* __restrict__ Wlo,
     const float* __restrict__ bias, void* __restrict__ C, int ldc, unsigned int* err) {
@@ -103,9 +110,9 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemm_tc3_kernel(
   const int ar = tid >> 2, ac = (tid & 3) * 16;
   const int64_t arow = m0 + ar;
   for (int ka = 0; ka < nk; ++ka) {
-    const int s = ka & 1;
+    const int s = ka % kGtStages;
     unsigned char* st = sm + s * kGtStage;
-    if (ka >= 2) {   // stage s was last read by the products of atom ka - 2
+    if (ka >= kGtStages) {   // stage s was last read by the products of atom ka - kGtStages
       if (!mbar_wait(&bar_mma[s], ph_m[s], err)) ok = false;
       ph_m[s] ^= 1;
       tc_fence_after();
@@ -160,7 +167,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemm_tc3_kernel(
   }
   // the last commit covers every product of thread 0
   {
-    const int s = (nk - 1) & 1;
+    const int s = (nk - 1) % kGtStages;
     if (!mbar_wait(&bar_mma[s], ph_m[s], err)) ok = false;
     tc_fence_after();
   }
