@@ -43,10 +43,6 @@ __device__ __forceinline__ uint32_t idesc_h(int M, int N) {
   return idesc_bf16(M, N) & ~((7u << 7) | (7u << 10));
 }
 
-__device__ __forceinline__ float h2f(uint16_t v) {
-  return __half2float(__ushort_as_half(v));
-}
-
 // ---------------------------------------------------------------------------
 // Slot kernel
 // ---------------------------------------------------------------------------
@@ -69,12 +65,15 @@ constexpr uint32_t kSOffStab = kSOffG + 2 * kGBytes;   // fp32 [22,128] (row 21 
 constexpr uint32_t kSOffSrc = kSOffStab + (kV + 1) * kH * 4; // per group, 2 buffers: [96] row pointers
 constexpr uint32_t kSOffSt = kSOffSrc + 4 * kSubN * 8; // per group, 2 buffers: [96] Stab row
 constexpr uint32_t kSOffJ = kSOffSt + 4 * kSubN * 4;   // int [48] local neighbour
-constexpr uint32_t kSlotSmem = kSOffJ + kK * 4 + 1024;
+constexpr uint32_t kSOffD1 = kSOffJ + kK * 4;          // fp32 [48][128] D1, slot-major
+constexpr uint32_t kSOffAS = kSOffD1 + kK * kH * 4;    // per group, 2 buffers: fp32 [2][128] A rows
+constexpr uint32_t kSlotSmem = kSOffAS + 4 * kSubRows * kH * 4 + 1024;
+static_assert(kSlotSmem <= 227 * 1024, "slot kernel shared memory");
 constexpr uint32_t kTfColD2 = 64;                  // group g: columns 64 + 96 g
 constexpr int kGroupThreadsTf = 256;
 
 // The V row of a slot past K (its products are dropped by the slot sum).
-__device__ const uint16_t g_zero_row[kH] = {};
+__device__ __align__(16) const uint16_t g_zero_row[kH] = {};
 
 __device__ __forceinline__ void load_etile(unsigned char* tile, const uint16_t* h_e, int64_t row0,
                                            int64_t row_end, int tid) {
@@ -91,6 +90,7 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
   unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float* StabS = reinterpret_cast<float*>(sm + kSOffStab);
   int* SJ = reinterpret_cast<int*>(sm + kSOffJ);
+  float* D1s = reinterpret_cast<float*>(sm + kSOffD1);
   __shared__ uint64_t bar_w, bar_d1, bar_d2[2];
   __shared__ uint32_t tmem_base;
 
@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
   const uint16_t** SRC0 = reinterpret_cast<const uint16_t**>(sm + kSOffSrc) + grp * 2 * kSubN;
   int* STR0 = reinterpret_cast<int*>(sm + kSOffSt) + grp * 2 * kSubN;
   unsigned char* G = sm + kSOffG + grp * kGBytes;
+  float* AS0 = reinterpret_cast<float*>(sm + kSOffAS) + grp * 2 * kSubRows * kH;
   const uint16_t* PVl = l == 0 ? p.PVenc : p.PV;   // decoded neighbours' rows
 
   if (tid == 0) {
@@ -175,10 +176,20 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
     const int rn = r + gridDim.x;
     if (rn < R) load_etile(sm + kSOffE + ((it + 1) & 1) * kETileBytes, p.h_e, (int64_t)rn * kK, SL, tid);
     cp_async_commit();
-    float d1[kK];
-    tmem_ld48(tm + lane_base, d1);
+    // D1 to shared memory, slot-major (D1s[k][f]): warp w reads its lane
+    // quadrant's features for slots 12 (w / 4) .. 12 (w / 4) + 11
+    {
+      const int k0 = (warp >> 2) * 12;
+      float v8[8], v4[4];
+      tmem_ld8(tm + lane_base + (uint32_t)k0, v8);
+      tmem_ld4(tm + lane_base + (uint32_t)(k0 + 8), v4);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) D1s[(k0 + i) * kH + f] = v8[i];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) D1s[(k0 + 8 + i) * kH + f] = v4[i];
+    }
     tc_fence_before();
-    __syncthreads();   // SJ visible; D1 read by every thread before the next item's MMA
+    __syncthreads();   // SJ and D1s visible; D1 read before the next item's MMA
     // Gather addresses of sub-tile `sub` into address buffer `ab` (threads
     // gtid < 96 of the group; their global loads overlap the group's MMA).
     // Per slot of sub-tile `sub`: the address of its V row (a decoded
@@ -206,6 +217,16 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
         }
         SRC0[ab * kSubN + gtid] = src;
         STR0[ab * kSubN + gtid] = st;
+      } else if (gtid >= kSubN && gtid < kSubN + kSubRows * 32 && sub * kSubRows < nseq) {
+        // the sub-tile's A rows (W1a h + b1 of each row, fp32) into AS[ab]
+        const int s0 = sub * kSubRows;
+        const int rr = (gtid - kSubN) >> 5, c4 = (gtid - kSubN) & 31;
+        if (s0 + rr < nseq) {
+          const float* arow = l == 0 ? p.Aenc0 + (int64_t)r * kH
+                                     : p.A + (p.bv.seq_row_off[seq0 + s0 + rr] + t) * kH;
+          reinterpret_cast<float4*>(AS0 + (ab * kSubRows + rr) * kH)[c4] =
+              reinterpret_cast<const float4*>(arow)[c4];
+        }
       }
     };
     stage(grp, 0);
@@ -215,36 +236,48 @@ __global__ void __launch_bounds__(kTfThreads, 1) tf_slot_tc_kernel(const __grid_
       const int s0 = sub * kSubRows;
       const int nrows = nseq - s0 < kSubRows ? nseq - s0 : kSubRows;
       const int N = nrows * kK;
-      const uint16_t* const* SRC = SRC0 + ab * kSubN + rho * kK;
-      const int* STR = STR0 + ab * kSubN + rho * kK;
-      int64_t q = -1;
-      if (rho < nrows) {
-        const int64_t qs = p.bv.seq_row_off[seq0 + s0 + rho];
-        q = qs + t;
-        const float a = l == 0 ? p.Aenc0[(int64_t)r * kH + f] : p.A[q * kH + f];
-        // this thread's column of the SW128 operand: row (slot) k of this
-        // row's 48 is at gcol + (k / 8) * 1024 + (k % 8) * 128 + ((c ^ k % 8) << 4)
-        unsigned char* gcol = G + (f >> 6) * N * 128 + rho * kK * 128 + (f & 7) * 2;
-        const int c = (f & 63) >> 3;
-        const float* stf = StabS + f;
+      int64_t q = -1;   // the row this thread sums (feature f of row rho)
+      if (rho < nrows) q = p.bv.seq_row_off[seq0 + s0 + rho] + t;
+      // Build: thread (c8, r0) forms 8 consecutive features (8 c8 ..) of slot
+      // rows r0, r0 + 16, ..., r0 + 80 of the sub-tile (row r = 48 rr + k):
+      // 2 GELU(D1[k] + A_rr + V + W1c W_s[tok]) in fp32, one 16-byte fp16
+      // store into the SW128 operand.  Slots past K get zeros (the slot sum
+      // drops their products).
+      {
+        const int c8 = gtid & 15, r0 = gtid >> 4;
+        const uint16_t* const* SRC = SRC0 + ab * kSubN;
+        const int* STR = STR0 + ab * kSubN;
+        const float* AS = AS0 + ab * kSubRows * kH;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          // 24 slots: all gathers first, then the GELUs
-          uint16_t raw[24];
+        for (int i = 0; i < kSubN / 16; ++i) {
+          const int rs = r0 + 16 * i;
+          const int rr = rs / kK, k = rs % kK;
+          if (rr >= nrows) continue;
+          uint4 outv = make_uint4(0, 0, 0, 0);
+          if (k < K) {
+            const uint4 vr = *reinterpret_cast<const uint4*>(SRC[rs] + c8 * 8);
+            const float4* d = reinterpret_cast<const float4*>(D1s + k * kH + c8 * 8);
+            const float4* av = reinterpret_cast<const float4*>(AS + rr * kH + c8 * 8);
+            const float4* sv = reinterpret_cast<const float4*>(StabS + STR[rs] + c8 * 8);
+            const float4 d0 = d[0], d1v = d[1], a0 = av[0], a1 = av[1], t0 = sv[0], t1 = sv[1];
+            const float dd[8] = {d0.x, d0.y, d0.z, d0.w, d1v.x, d1v.y, d1v.z, d1v.w};
+            const float aa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float tt[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+            const uint32_t vw[4] = {vr.x, vr.y, vr.z, vr.w};
+            uint32_t pk[4];
 #pragma unroll
-          for (int u = 0; u < 24; ++u) raw[u] = SRC[h * 24 + u][f];
-#pragma unroll
-          for (int u = 0; u < 24; u += 2) {
-            const int k = h * 24 + u;
-            const float x0 = d1[k] + a + h2f(raw[u]) + stf[STR[k]];
-            const float x1 = d1[k + 1] + a + h2f(raw[u + 1]) + stf[STR[k + 1]];
-            // the operand holds 2 GELU(x); the epilogue halves D2 (exact)
-            const float2 y = gelu2_tc_x2(make_float2(x0, x1));
-            *reinterpret_cast<__half*>(gcol + (k >> 3) * 1024 + (k & 7) * 128 +
-                                       ((c ^ (k & 7)) << 4)) = __float2half_rn(y.x);
-            *reinterpret_cast<__half*>(gcol + ((k + 1) >> 3) * 1024 + ((k + 1) & 7) * 128 +
-                                       ((c ^ ((k + 1) & 7)) << 4)) = __float2half_rn(y.y);
+            for (int u = 0; u < 4; ++u) {
+              const float2 vv = __half22float2(*reinterpret_cast<const __half2*>(&vw[u]));
+              const float x0 = ((dd[2 * u] + aa[2 * u]) + vv.x) + tt[2 * u];
+              const float x1 = ((dd[2 * u + 1] + aa[2 * u + 1]) + vv.y) + tt[2 * u + 1];
+              // the operand holds 2 GELU(x); the epilogue halves D2 (exact)
+              const float2 y = gelu2_tc_x2(make_float2(x0, x1));
+              const __half2 h = __floats2half2_rn(y.x, y.y);
+              pk[u] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            outv = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
+          *reinterpret_cast<uint4*>(G + sw128_offset(rs, c8 * 8, N)) = outv;
         }
       }
       fence_async_smem();
