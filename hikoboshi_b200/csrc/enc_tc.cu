@@ -330,6 +330,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float (*red)[4][128] = reinterpret_cast<float (*)[4][128]>(sm + kEdgeOffRed);
   __shared__ uint64_t bar_w, bar_mma, bar_r[2];
+  __shared__ unsigned char vrow[128];   // tile rows with a valid neighbour
   __shared__ uint32_t tmem_base;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -444,6 +445,12 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       const int64_t tn = t + gridDim.x;
       if (tn < tiles) load_rows_async(atile, p.h_e, tn * 128, SL, 128, tid);
       cp_async_commit();
+      // The next tile's remainder rows (read only as its residual, so never
+      // brought in by anything else) into L2 a whole tile ahead.
+      if (tid == 0 && tn < tiles) {
+        const int64_t rows = SL - tn * 128 < 128 ? SL - tn * 128 : 128;
+        bulk_prefetch_l2(p.h_e_lo + tn * 128 * kH, (uint32_t)(rows * kH * 2));
+      }
     }
     // epilogue 1: G = GELU(D1 + N_i + N_j) on this thread's 32 columns
     {
@@ -569,7 +576,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       const float var =
           (red[1][0][row] + red[1][1][row] + red[1][2][row] + red[1][3][row]) * (1.0f / 128.0f);
       const float inv = 1.0f / sqrtf(var + kLnEps);
-      if (rj >= 0) {
+      {
         const float4* gw = reinterpret_cast<const float4*>(p.n3w + c0);   // warp-uniform
         const float4* gb = reinterpret_cast<const float4*>(p.n3b + c0);
 #pragma unroll
@@ -580,7 +587,44 @@ __global__ void __launch_bounds__(kEncThreads, 1)
           x[4 * q + 2] = x[4 * q + 2] * inv * g.z + b.z;
           x[4 * q + 3] = x[4 * q + 3] * inv * g.w + b.w;
         }
-        store_hi_lo(p.h_e_out + s * kH + c0, p.h_e_lo + s * kH + c0, x);
+      }
+      // Store through G (free since MMA3 completed): a thread owns 32
+      // columns of one row, so direct stores would touch 32 rows per warp
+      // instruction; staged, each warp instruction writes two contiguous
+      // 256-byte rows.  Value first, then remainder; rows without a valid
+      // neighbour are not written (edge_update keeps them).
+      uint32_t ph[16], pl[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const __half2 h = __floats2half2_rn(x[2 * q], x[2 * q + 1]);
+        const float2 hf = __half22float2(h);
+        ph[q] = *reinterpret_cast<const uint32_t*>(&h);
+        const __half2 l = __floats2half2_rn(x[2 * q] - hf.x, x[2 * q + 1] - hf.y);
+        pl[q] = *reinterpret_cast<const uint32_t*>(&l);
+      }
+      if (cg == 0) vrow[row] = rj >= 0 ? 1 : 0;
+      __syncthreads();   // every read of red[] (which lives in G) is done
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const uint32_t* pk = half ? pl : ph;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int cc = cg * 4 + u;
+          *reinterpret_cast<uint4*>(G + row * 256 + ((cc ^ (row & 15)) << 4)) =
+              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+        __syncthreads();
+        uint16_t* out = half ? p.h_e_lo : p.h_e_out;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int idx = tid + kEncThreads * i;
+          const int rr = idx >> 4, cc = idx & 15;
+          const int64_t so = t * 128 + rr;
+          if (so < SL && vrow[rr])
+            *reinterpret_cast<uint4*>(out + so * kH + cc * 8) =
+                *reinterpret_cast<const uint4*>(G + rr * 256 + ((cc ^ (rr & 15)) << 4));
+        }
+        __syncthreads();
       }
     }
     tc_fence_before();
