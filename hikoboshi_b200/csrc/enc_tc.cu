@@ -66,28 +66,6 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// 32 consecutive h_E values of one row stored as fp16 (hi, the MMA operand)
-// and fp16 remainders (lo): hi + lo keeps about 22 significant bits of the
-// residual stream between the encoder layers.
-__device__ __forceinline__ void store_hi_lo(uint16_t* hi, uint16_t* lo, const float (&x)[32]) {
-  uint32_t ph[16], pl[16];
-#pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    const __half2 h = __floats2half2_rn(x[2 * q], x[2 * q + 1]);
-    const float2 hf = __half22float2(h);
-    ph[q] = *reinterpret_cast<const uint32_t*>(&h);
-    const __half2 l = __floats2half2_rn(x[2 * q] - hf.x, x[2 * q + 1] - hf.y);
-    pl[q] = *reinterpret_cast<const uint32_t*>(&l);
-  }
-  uint4* dh = reinterpret_cast<uint4*>(hi);
-  uint4* dl = reinterpret_cast<uint4*>(lo);
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    dh[u] = make_uint4(ph[4 * u], ph[4 * u + 1], ph[4 * u + 2], ph[4 * u + 3]);
-    dl[u] = make_uint4(pl[4 * u], pl[4 * u + 1], pl[4 * u + 2], pl[4 * u + 3]);
-  }
-}
-
 // fp16 pair of (a, b) or, with lo, of their remainders a - fp16(a), b - fp16(b)
 // (exact in fp32): an operand x = hi + lo applied by two MMAs into one
 // accumulator carries about twice the fp16 precision.
@@ -867,13 +845,47 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       }
     }
     {
-      const int64_t s = t * 128 + row;
       float v[32];
       tmem_ld32(tm + lane_base + 128u + (uint32_t)c0, v);
-      if (s < SL) {
+      const float4* wb = reinterpret_cast<const float4*>(p.We_b + c0);   // warp-uniform
 #pragma unroll
-        for (int q = 0; q < 32; ++q) v[q] += p.We_b[c0 + q];
-        store_hi_lo(p.h_e + s * kH + c0, p.h_e_lo + s * kH + c0, v);
+      for (int q = 0; q < 8; ++q) {
+        const float4 b = wb[q];
+        v[4 * q] += b.x;
+        v[4 * q + 1] += b.y;
+        v[4 * q + 2] += b.z;
+        v[4 * q + 3] += b.w;
+      }
+      // h_E value, then remainder, through the operand buffer (free: the
+      // W_e products have completed) so each warp instruction stores two
+      // contiguous 256-byte rows
+      uint32_t ph[16], pl[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        ph[q] = pack_h2s(v[2 * q], v[2 * q + 1], false);
+        pl[q] = pack_h2s(v[2 * q], v[2 * q + 1], true);
+      }
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const uint32_t* pk = half ? pl : ph;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int cc = cg * 4 + u;
+          *reinterpret_cast<uint4*>(A + row * 256 + ((cc ^ (row & 15)) << 4)) =
+              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+        __syncthreads();
+        uint16_t* out = half ? p.h_e_lo : p.h_e;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int idx = tid + kEncThreads * i;
+          const int rr = idx >> 4, cc = idx & 15;
+          const int64_t so = t * 128 + rr;
+          if (so < SL)
+            *reinterpret_cast<uint4*>(out + so * kH + cc * 8) =
+                *reinterpret_cast<const uint4*>(A + rr * 256 + ((cc ^ (rr & 15)) << 4));
+        }
+        __syncthreads();
       }
     }
     tc_fence_before();
