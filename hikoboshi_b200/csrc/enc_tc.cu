@@ -25,9 +25,10 @@
 //
 //   enc_featurize_tc: edge features -> W_edge -> LN -> W_e, described below.
 //
-// All are persistent (one CTA per SM, 16 warps).  Weight images stay resident
-// in shared memory (bulk copies; the edge pass streams its remainder images
-// through a 2-slot ring), the next tile's h_E rows are fetched by cp.async as
+// All are persistent (one CTA per SM, 16 warps).  Weight images arrive by bulk
+// copies: the node pass and the featurisation keep theirs resident, the edge
+// pass streams its six images through a 3-slot ring and uses the space to
+// stage its row gathers.  The next tile's h_E rows are fetched by cp.async as
 // soon as the current tile's first MMA has read them, node terms are gathered
 // while MMAs run, and a tile's MMAs are issued by thread 0 and
 // completion-tracked on one mbarrier.  Every wait is bounded.
@@ -292,14 +293,22 @@ __global__ void __launch_bounds__(kEncThreads, 1)
 // Edge-update kernel: 128 slots per tile.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kEdgeTileBytes = 128 * 256;             // 32 KiB
-// W11b, W12, W13 stay resident; their fp16 remainders (W - hi) stream through
-// a 2-slot ring in the order the MMAs use them (W11b, W12, W13 per tile).
-constexpr uint32_t kEdgeOffW = 0;                          // W11b, W12, W13
-constexpr uint32_t kEdgeOffR = 3 * kW128Bytes;             // remainder ring, 2 slots
-constexpr uint32_t kEdgeOffA = kEdgeOffR + 2 * kW128Bytes; // h_E tile
-constexpr uint32_t kEdgeOffG = kEdgeOffA + kEdgeTileBytes;
+// The six weight images (W11b, W12, W13, each as fp16 value and fp16
+// remainder W - hi) stream through a 3-slot ring in the order the MMAs use
+// them; a tile consumes ring entries 6i .. 6i+5.  X stages gathered rows so
+// that every global load of the pass reads whole rows per warp instruction:
+// the neighbour node terms W11c h_j (fp32 [128][128]) while D1 runs, then the
+// tile's residual h_E (fp16 value and remainder, [128][128] each) from
+// epilogue 1 to epilogue 3, then the LayerNorm output for the store.  A
+// thread owns one TMEM row (slot) and 32 columns, so loading its own row
+// pieces directly would touch 32 rows per warp instruction.
+constexpr int kEdgeRing = 3;
+constexpr uint32_t kEdgeOffW = 0;                                   // weight ring
+constexpr uint32_t kEdgeOffA = kEdgeRing * kW128Bytes;              // h_E tile (MMA operand)
+constexpr uint32_t kEdgeOffG = kEdgeOffA + kEdgeTileBytes;          // GELU operand
 constexpr uint32_t kEdgeOffRed = kEdgeOffG;   // float [2][4][128], used when G is free
-constexpr uint32_t kEdgeSmem = kEdgeOffG + kEdgeTileBytes + 1024;
+constexpr uint32_t kEdgeOffX = kEdgeOffG + kEdgeTileBytes;          // 64 KiB staging
+constexpr uint32_t kEdgeSmem = kEdgeOffX + 2 * kEdgeTileBytes + 1024;
 static_assert(kEdgeSmem <= 227 * 1024, "edge kernel shared memory");
 
 __global__ void __launch_bounds__(kEncThreads, 1)
@@ -307,8 +316,11 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float (*red)[4][128] = reinterpret_cast<float (*)[4][128]>(sm + kEdgeOffRed);
-  __shared__ uint64_t bar_w, bar_mma, bar_r[2];
-  __shared__ unsigned char vrow[128];   // tile rows with a valid neighbour
+  unsigned char* X = sm + kEdgeOffX;
+  __shared__ uint64_t bar_mma, bar_w[kEdgeRing];
+  // global residue row of each tile row's neighbour (-1: none); [it & 1] is
+  // the current tile, the other buffer is filled for the next one
+  __shared__ int SJ[2][128];
   __shared__ uint32_t tmem_base;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -320,114 +332,161 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   const int64_t SL = (int64_t)R * kK;
   const int64_t tiles = (SL + 127) / 128;
 
+  int64_t t = blockIdx.x;
   if (tid == 0) {
-    mbar_init(&bar_w, 1);
     mbar_init(&bar_mma, 1);
-    mbar_init(&bar_r[0], 1);
-    mbar_init(&bar_r[1], 1);
+    for (int i = 0; i < kEdgeRing; ++i) mbar_init(&bar_w[i], 1);
     fence_barrier_init();
   }
   if (warp == 0) {
     tmem_alloc(&tmem_base, 256);
     tmem_relinquish();
   }
+  // neighbour rows of this CTA's first tile
+  if (tid < 128) {
+    const int64_t s = t * 128 + tid;
+    int rj = -1;
+    if (s < SL) {
+      const int r = (int)(s / kK), k = (int)(s % kK);
+      const int b = p.bv.res_prot[r];
+      const int L = p.bv.prot_len[b];
+      const int j = k < (L < kK ? L : kK) ? p.e_idx[s] : -1;
+      if (j >= 0 && j < L) rj = p.bv.prot_res_off[b] + j;
+    }
+    SJ[0][tid] = rj;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tmem_base;
-  // remainder-ring state (thread 0): entry j is remainder j % 3 of this CTA's
-  // tile j / 3, in slot j % 2
-  const unsigned char* rem[3] = {p.W11b_lo, p.W12_lo, p.W13_lo};
-  const int64_t my_tiles =
-      (int64_t)blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int64_t r_total = my_tiles * 3;
-  auto rem_issue = [&](int64_t j) {
-    if (j >= r_total) return;
-    uint64_t* b = &bar_r[j & 1];
-    mbar_arrive_expect_tx(b, kW128Bytes);
-    for (uint32_t o = 0; o < kW128Bytes; o += 16384u)
-      bulk_g2s(sm + kEdgeOffR + (j & 1) * kW128Bytes + o, rem[j % 3] + o, 16384u, b);
+
+  // weight ring (thread 0): entry j is image j % 6 of this CTA's tile j / 6,
+  // in slot j % 3; it is issued once entry j - 3's MMAs have completed.
+  const int my_tiles =
+      (int)((int64_t)blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0);
+  const int w_total = my_tiles * 6;
+  int w_issued = 0, w_landed = 0;   // entries issued / waited for successfully
+  auto w_img = [&](int i) -> const unsigned char* {
+    switch (i) {
+      case 0: return p.W11b;
+      case 1: return p.W11b_lo;
+      case 2: return p.W12;
+      case 3: return p.W12_lo;
+      case 4: return p.W13;
+      default: return p.W13_lo;
+    }
   };
-  auto rem_wait = [&](int64_t j, bool& okf) {
-    if (!mbar_wait(&bar_r[j & 1], (uint32_t)((j >> 1) & 1), p.err)) okf = false;
-    return smem_u32(sm + kEdgeOffR + (j & 1) * kW128Bytes);
+  auto w_issue = [&](int j) {
+    if (j >= w_total) return;
+    const int slot = j % kEdgeRing;
+    mbar_arrive_expect_tx(&bar_w[slot], kW128Bytes);
+    const unsigned char* img = w_img(j % 6);
+    for (uint32_t o = 0; o < kW128Bytes; o += 16384u)
+      bulk_g2s(sm + kEdgeOffW + slot * kW128Bytes + o, img + o, 16384u, &bar_w[slot]);
+    w_issued = j + 1;
+  };
+  auto w_wait = [&](int j, bool& okf) -> uint32_t {
+    const int slot = j % kEdgeRing;
+    if (mbar_wait(&bar_w[slot], (uint32_t)((j / kEdgeRing) & 1), p.err)) w_landed = j + 1;
+    else okf = false;
+    return smem_u32(sm + kEdgeOffW + slot * kW128Bytes);
   };
   if (tid == 0) {
-    const unsigned char* imgs[3] = {p.W11b, p.W12, p.W13};
-    load_weights(sm + kEdgeOffW, imgs, 3, &bar_w);
-    rem_issue(0);
-    rem_issue(1);
+    w_issue(0);
+    w_issue(1);
+    w_issue(2);
   }
   bool ok = true;
-  if (!mbar_wait(&bar_w, 0, p.err)) ok = false;
   uint32_t ph = 0;
   const uint32_t idesc = idesc_f16(128, 128);
   unsigned char* G = sm + kEdgeOffG;
+  // the next tile's neighbour-index chain (threads 0..127), loaded in three
+  // steps spread over the current tile so that no load is waited for
+  int nx_e = -1, nx_b = 0, nx_L = 0, nx_off = 0;
 
-  int64_t t = blockIdx.x;
   if (t < tiles) load_rows_async(sm + kEdgeOffA, p.h_e, t * 128, SL, 128, tid);
   cp_async_commit();
-  int64_t rj0 = 0;   // remainder entry of this tile's first MMA
-  for (int it = 0; t < tiles; t += gridDim.x, ++it, rj0 += 3) {
+  for (int it = 0; t < tiles; t += gridDim.x, ++it) {
     if (__syncthreads_or(!ok)) break;
+    const int j0 = 6 * it;
+    const int* sj = SJ[it & 1];
     unsigned char* atile = sm + kEdgeOffA;
     cp_async_wait_all();
     fence_async_smem();
     __syncthreads();
     if (tid == 0) {
       // each weight as hi + remainder: two MMAs into one accumulator
+      uint32_t w = w_wait(j0, ok);
       tc_fence_after();
-      mma_k128(tm, smem_u32(atile), smem_u32(sm + kEdgeOffW), 128, idesc, false);
-      const uint32_t r = rem_wait(rj0, ok);
+      mma_k128(tm, smem_u32(atile), w, 128, idesc, false);
+      w = w_wait(j0 + 1, ok);
       tc_fence_after();
-      mma_k128(tm, smem_u32(atile), r, 128, idesc, true);
+      mma_k128(tm, smem_u32(atile), w, 128, idesc, true);
       mma_commit(&bar_mma);
     }
-    // this thread's slot
-    const int64_t s = t * 128 + row;
-    int r = 0, rj = -1;
-    if (s < SL) {
-      r = (int)(s / kK);
-      const int k = (int)(s % kK);
-      const int b = p.bv.res_prot[r];
-      const int L = p.bv.prot_len[b];
-      const int K = L < kK ? L : kK;
-      const int j = k < K ? p.e_idx[s] : -1;
-      if (j >= 0 && j < L) rj = p.bv.prot_res_off[b] + j;
+    // The tile rows' neighbour terms W11c h_j (512 B per row) into X while the
+    // D1 MMAs run: chunk e = tid + 512 i is 16-byte chunk e & 31 of row e >> 5,
+    // so each warp instruction reads one whole row; rows without a neighbour
+    // are zero-filled.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = tid + kEncThreads * i;
+      const int rr = e >> 5, cc = e & 31;
+      const int rj = sj[rr];
+      const float* src = p.NAC + (rj >= 0 ? (int64_t)rj * 256 + 128 + cc * 4 : 0);
+      cp_async16(X + rr * 512 + ((cc ^ (rr & 7)) << 4), src, rj >= 0);
     }
-    // the slot's node terms [W11a h_i + b11] + W11c h_j on this thread's 32
-    // columns, gathered while the D1 MMAs run
+    cp_async_commit();
+    // this thread's slot; its own node term [W11a h_i + b11] (the slots of a
+    // warp span at most two residues, so these loads are near-broadcasts)
+    const int64_t s = t * 128 + row;
+    const int rj = sj[row];
     float nsum[32];
-    if (rj >= 0) {
+    {
+      const int r = (int)((s < SL ? s : 0) / kK);
       const float4* na = reinterpret_cast<const float4*>(p.NAC + (int64_t)r * 256 + c0);
-      const float4* nc = reinterpret_cast<const float4*>(p.NAC + (int64_t)rj * 256 + 128 + c0);
+      float4 a[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) a[q] = na[q];
+      cp_async_wait_all();
+      __syncthreads();
+      const unsigned char* xr = X + row * 512;
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const float4 a = na[q], c = nc[q];
-        nsum[4 * q] = a.x + c.x;
-        nsum[4 * q + 1] = a.y + c.y;
-        nsum[4 * q + 2] = a.z + c.z;
-        nsum[4 * q + 3] = a.w + c.w;
+        const float4 c =
+            *reinterpret_cast<const float4*>(xr + (((cg * 8 + q) ^ (row & 7)) << 4));
+        nsum[4 * q] = a[q].x + c.x;
+        nsum[4 * q + 1] = a[q].y + c.y;
+        nsum[4 * q + 2] = a[q].z + c.z;
+        nsum[4 * q + 3] = a[q].w + c.w;
       }
-    } else {
-#pragma unroll
-      for (int q = 0; q < 32; ++q) nsum[q] = 0.0f;
     }
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
-    // D1's MMAs are complete: the h_E tile and the first remainder slot are
-    // free, so the next tile's rows and the next remainder load meanwhile.
-    if (tid == 0) rem_issue(rj0 + 2);
+    // D1's MMAs are complete: the h_E tile and entries j0, j0 + 1 are free,
+    // so the next tile's rows and weight entries load meanwhile.
+    if (tid == 0) {
+      w_issue(j0 + 3);
+      w_issue(j0 + 4);
+    }
+    const int64_t tn = t + gridDim.x;
     {
-      const int64_t tn = t + gridDim.x;
       if (tn < tiles) load_rows_async(atile, p.h_e, tn * 128, SL, 128, tid);
       cp_async_commit();
-      // The next tile's remainder rows (read only as its residual, so never
-      // brought in by anything else) into L2 a whole tile ahead.
+      // The next tile's remainder rows into L2 a whole tile ahead of its
+      // residual staging.
       if (tid == 0 && tn < tiles) {
         const int64_t rows = SL - tn * 128 < 128 ? SL - tn * 128 : 128;
         bulk_prefetch_l2(p.h_e_lo + tn * 128 * kH, (uint32_t)(rows * kH * 2));
+      }
+    }
+    if (tid < 128) {   // next tile's index chain, step 1
+      nx_e = -1;
+      const int64_t sn = tn * 128 + tid;
+      if (tn < tiles && sn < SL) {
+        nx_b = p.bv.res_prot[(int)(sn / kK)];
+        nx_e = p.e_idx[sn];
       }
     }
     // epilogue 1: G = GELU(D1 + N_i + N_j) on this thread's 32 columns
@@ -456,16 +515,38 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma_k128(tm + 128, smem_u32(G), smem_u32(sm + kEdgeOffW + kW128Bytes), 128, idesc, false);
-      const uint32_t r = rem_wait(rj0 + 1, ok);
+      uint32_t w = w_wait(j0 + 2, ok);
       tc_fence_after();
-      mma_k128(tm + 128, smem_u32(G), r, 128, idesc, true);
+      mma_k128(tm + 128, smem_u32(G), w, 128, idesc, false);
+      w = w_wait(j0 + 3, ok);
+      tc_fence_after();
+      mma_k128(tm + 128, smem_u32(G), w, 128, idesc, true);
       mma_commit(&bar_mma);
+    }
+    // The tile's residual rows, value then remainder (fp16, 256 B each), into
+    // X: every thread has read its node terms (barrier above).  Chunk
+    // e = tid + 512 i: array e >> 11, row (e >> 4) & 127, 16-byte chunk e & 15.
+    // They land during D2 and epilogue 2 and are waited for before D3.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = tid + kEncThreads * i;
+      const int half = e >> 11, rr = (e >> 4) & 127, cc = e & 15;
+      const int64_t so = t * 128 + rr;
+      const uint16_t* src = (half ? p.h_e_lo : p.h_e) + (so < SL ? so : 0) * kH + cc * 8;
+      cp_async16(X + half * kEdgeTileBytes + rr * 256 + ((cc ^ (rr & 15)) << 4), src, so < SL);
+    }
+    cp_async_commit();
+    if (tid < 128 && nx_e >= 0) {   // next tile's index chain, step 2
+      nx_L = p.bv.prot_len[nx_b];
+      nx_off = p.bv.prot_res_off[nx_b];
     }
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
-    if (tid == 0) rem_issue(rj0 + 3);
+    if (tid == 0) {
+      w_issue(j0 + 5);
+      w_issue(j0 + 6);
+    }
     // epilogue 2: G = GELU(D2 + b12)   (G was consumed by the MMA above)
     {
       float v[32];
@@ -485,35 +566,27 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         *reinterpret_cast<uint4*>(G + sw128_offset(row, c0 + 8 * u, 128)) =
             make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
     }
+    cp_async_wait_all();   // residual rows (and the next tile's h_E rows)
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma_k128(tm, smem_u32(G), smem_u32(sm + kEdgeOffW + 2 * kW128Bytes), 128, idesc, false);
-      const uint32_t r = rem_wait(rj0 + 2, ok);
+      uint32_t w = w_wait(j0 + 4, ok);
       tc_fence_after();
-      mma_k128(tm, smem_u32(G), r, 128, idesc, true);
+      mma_k128(tm, smem_u32(G), w, 128, idesc, false);
+      w = w_wait(j0 + 5, ok);
+      tc_fence_after();
+      mma_k128(tm, smem_u32(G), w, 128, idesc, true);
       mma_commit(&bar_mma);
-    }
-    // the residual h_E row as its fp16 value plus fp16 remainder (the tile
-    // buffer already holds the next tile's rows; this row sits in L2), loaded
-    // while the W13 MMAs run
-    uint4 hres[4], lres[4];
-    {
-      const int64_t srow = (s < SL ? s : 0) * kH + c0;
-      const uint4* hrow = reinterpret_cast<const uint4*>(p.h_e + srow);
-      const uint4* lrow = reinterpret_cast<const uint4*>(p.h_e_lo + srow);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        hres[u] = hrow[u];
-        lres[u] = lrow[u];
-      }
     }
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
-    if (tid == 0) rem_issue(rj0 + 4);
+    if (tid == 0) {
+      w_issue(j0 + 7);
+      w_issue(j0 + 8);
+    }
     // epilogue 3: x = h_E + D3 + b13, LayerNorm over the row's 128 features
     // (four 32-column parts held by warps quad, quad+4, quad+8, quad+12)
     {
@@ -522,7 +595,9 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       const float2* b13 = reinterpret_cast<const float2*>(p.b13 + c0);   // warp-uniform
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const uint4 hv = hres[u], lv = lres[u];
+        const int co = ((cg * 4 + u) ^ (row & 15)) << 4;
+        const uint4 hv = *reinterpret_cast<const uint4*>(X + row * 256 + co);
+        const uint4 lv = *reinterpret_cast<const uint4*>(X + kEdgeTileBytes + row * 256 + co);
         const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w}, lw[4] = {lv.x, lv.y, lv.z, lv.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -566,53 +641,57 @@ __global__ void __launch_bounds__(kEncThreads, 1)
           x[4 * q + 3] = x[4 * q + 3] * inv * g.w + b.w;
         }
       }
-      // Store through G (free since MMA3 completed): a thread owns 32
-      // columns of one row, so direct stores would touch 32 rows per warp
-      // instruction; staged, each warp instruction writes two contiguous
-      // 256-byte rows.  Value first, then remainder; rows without a valid
-      // neighbour are not written (edge_update keeps them).
-      uint32_t ph[16], pl[16];
+      uint32_t pv[16], pl[16];
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
         const __half2 h = __floats2half2_rn(x[2 * q], x[2 * q + 1]);
         const float2 hf = __half22float2(h);
-        ph[q] = *reinterpret_cast<const uint32_t*>(&h);
+        pv[q] = *reinterpret_cast<const uint32_t*>(&h);
         const __half2 l = __floats2half2_rn(x[2 * q] - hf.x, x[2 * q + 1] - hf.y);
         pl[q] = *reinterpret_cast<const uint32_t*>(&l);
       }
-      if (cg == 0) vrow[row] = rj >= 0 ? 1 : 0;
-      __syncthreads();   // every read of red[] (which lives in G) is done
+      __syncthreads();   // every read of the residual rows in X is done
+      // Value and remainder rows staged in X (same layout as the residual),
+      // then copied out as whole rows; rows without a valid neighbour are not
+      // written (edge_update keeps them).
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const uint32_t* pk = half ? pl : ph;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int cc = cg * 4 + u;
-          *reinterpret_cast<uint4*>(G + row * 256 + ((cc ^ (row & 15)) << 4)) =
-              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-        }
-        __syncthreads();
-        uint16_t* out = half ? p.h_e_lo : p.h_e_out;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int idx = tid + kEncThreads * i;
-          const int rr = idx >> 4, cc = idx & 15;
-          const int64_t so = t * 128 + rr;
-          if (so < SL && vrow[rr])
-            *reinterpret_cast<uint4*>(out + so * kH + cc * 8) =
-                *reinterpret_cast<const uint4*>(G + rr * 256 + ((cc ^ (rr & 15)) << 4));
-        }
-        __syncthreads();
+      for (int u = 0; u < 4; ++u) {
+        const int co = ((cg * 4 + u) ^ (row & 15)) << 4;
+        *reinterpret_cast<uint4*>(X + row * 256 + co) =
+            make_uint4(pv[4 * u], pv[4 * u + 1], pv[4 * u + 2], pv[4 * u + 3]);
+        *reinterpret_cast<uint4*>(X + kEdgeTileBytes + row * 256 + co) =
+            make_uint4(pl[4 * u], pl[4 * u + 1], pl[4 * u + 2], pl[4 * u + 3]);
       }
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int e = tid + kEncThreads * i;
+        const int half = e >> 11, rr = (e >> 4) & 127, cc = e & 15;
+        const int64_t so = t * 128 + rr;
+        uint16_t* out = half ? p.h_e_lo : p.h_e_out;
+        if (so < SL && sj[rr] >= 0)
+          *reinterpret_cast<uint4*>(out + so * kH + cc * 8) = *reinterpret_cast<const uint4*>(
+              X + half * kEdgeTileBytes + rr * 256 + ((cc ^ (rr & 15)) << 4));
+      }
+    }
+    // next tile's index chain, step 3: its neighbour rows, read after the
+    // barriers at the top of the next iteration
+    if (tid < 128) {
+      int rjn = -1;
+      if (nx_e >= 0) {
+        const int kn = (int)((tn * 128 + tid) % kK);
+        if (kn < (nx_L < kK ? nx_L : kK) && nx_e < nx_L) rjn = nx_off + nx_e;
+      }
+      SJ[(it + 1) & 1][tid] = rjn;
     }
     tc_fence_before();
   }
   cp_async_wait_all();
   // Drain: no bulk copy may be in flight when the CTA exits (entries issued
-  // but not consumed after an early exit).
+  // but not waited for after an early exit).
   if (tid == 0)
-    for (int64_t j = rj0; j < r_total && j < rj0 + 2; ++j)
-      mbar_wait(&bar_r[j & 1], (uint32_t)((j >> 1) & 1), p.err);
+    for (int j = w_landed; j < w_issued; ++j)
+      mbar_wait(&bar_w[j % kEdgeRing], (uint32_t)((j / kEdgeRing) & 1), p.err);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
