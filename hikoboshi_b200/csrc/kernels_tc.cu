@@ -414,6 +414,16 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       M.m_next[tid] = m;
     }
     __syncthreads();
+    // The next position's raw neighbour indices (one 192-byte e_idx row per
+    // sequence) into NbNext by cp.async; they land during layer 0's message
+    // phase and next_codes() turns them into codes (the Nb fill above has
+    // read NbNext already).
+    if (p + 1 < L && tid < n * (kK / 4)) {
+      const int s = tid / (kK / 4), c = tid % (kK / 4);
+      cp_async16(&NbNext[s][c * 4], a.e_idx + (int64_t)(M.off[s] + M.t_next[s]) * kK + c * 4,
+                 true);
+    }
+    cp_async_commit();
 
     // Row loads of one neighbour-slot chunk (a message group): a thread owns
     // one 8-feature column chunk (tid % 16) of six slot rows: the slot table
@@ -454,6 +464,12 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       unsigned char* dst = sm + kOffG1 + grp * kG1Bytes;
       const int c8 = tid & 15;
       const int r0 = gtid >> 4;
+      // one-sequence chunks: every row of this thread shares A_t's 8 features
+      float4 ca0 = make_float4(0.f, 0.f, 0.f, 0.f), ca1 = ca0;
+      if (kChunkSeqs == 1 && c < n) {
+        ca0 = reinterpret_cast<const float4*>(Aa[c])[c8 * 2];
+        ca1 = reinterpret_cast<const float4*>(Aa[c])[c8 * 2 + 1];
+      }
 #pragma unroll
       for (int i = 0; i < kRowsPerThread; ++i) {
         const int r = r0 + kRowStride * i;
@@ -473,8 +489,10 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
             s1 = st[1];
           }
           const float st8[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-          const float4 a0 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2];
-          const float4 a1 = reinterpret_cast<const float4*>(Aa[s])[c8 * 2 + 1];
+          const float4 a0 =
+              kChunkSeqs == 1 ? ca0 : reinterpret_cast<const float4*>(Aa[s])[c8 * 2];
+          const float4 a1 =
+              kChunkSeqs == 1 ? ca1 : reinterpret_cast<const float4*>(Aa[s])[c8 * 2 + 1];
           const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
           // the operand holds 2 GELU(x): the epilogue halves D2 when it adds
           // b2 (W2 is linear and a power-of-two scale is exact)
@@ -635,6 +653,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
         fence_async_smem();                     // slot sums feed the W3 MMA
       }
       ++tile;                                   // W2 consumed
+      if (l == 0) cp_async_wait_all();          // next position's e_idx rows
       __syncthreads();
       // every build of this layer is done: stage the next layer's table
       if (tid == 0 && (l < 2 || p + 1 < L) && !*abort_p) {
@@ -692,26 +711,45 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
       __syncthreads();
       // ---- layer 0, while the first W_in products run: the next position's
       // neighbour codes (its residue and mask were read at this position's
-      // set-up) and an L2 prefetch of its node rows; they are consumed after
-      // this position's sampling.
+      // set-up, its raw neighbour indices staged in NbNext then) and an L2
+      // prefetch of its node rows; they are consumed after this position's
+      // sampling.  The pos / tokens loads of a thread's entries are all
+      // issued before any is used: one global-load round trip.
       auto next_codes = [&]() {
-        for (int e = tid; e < n * kK; e += kThreadsB) {
+        constexpr int kPer = (kGB * kK + kThreadsB - 1) / kThreadsB;
+        int jj[kPer], ps[kPer], tk[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int e = tid + kThreadsB * i;
           const int s = e / kK, k = e % kK;
-          int code = 0;
-          if (k < K) {
-            const int tn = M.t_next[s];
-            int j = a.e_idx[(int64_t)(M.off[s] + tn) * kK + k];
+          jj[i] = -1;
+          ps[i] = 0;
+          tk[i] = 0;
+          if (e < n * kK && k < K) {
+            int j = NbNext[s][k];
             if (j < 0 || j >= L) {
               atomicOr(err, kErrBadIndex);
-              j = tn;
+              j = M.t_next[s];
             }
+            jj[i] = j;
             const int64_t qj = M.qrow[s] + j;
-            const int ps = a.pos[qj];
-            if (ps < p) code = j | (1 << 16) | (a.tokens[qj] << 17);
-            else if (ps == p) code = j | (1 << 16) | kFresh;   // decoded at this position
-            else code = j;
+            ps[i] = a.pos[qj];
+            tk[i] = a.tokens[qj];   // used only if decoded before this position
           }
-          NbNext[s][k] = code;
+        }
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int e = tid + kThreadsB * i;
+          if (e < n * kK) {
+            int code = 0;
+            const int j = jj[i];
+            if (j >= 0) {
+              if (ps[i] < p) code = j | (1 << 16) | (tk[i] << 17);
+              else if (ps[i] == p) code = j | (1 << 16) | kFresh;   // decoded at this position
+              else code = j;
+            }
+            NbNext[e / kK][e % kK] = code;
+          }
         }
         if (tid < n * 8) {
           const int s = tid >> 3, line = tid & 3;
