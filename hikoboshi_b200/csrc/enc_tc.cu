@@ -414,6 +414,20 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     cp_async_wait_all();
     fence_async_smem();
     __syncthreads();
+    // The tile rows' neighbour terms W11c h_j (512 B per row) into X while the
+    // D1 MMAs run: chunk e = tid + 512 i is 16-byte chunk e & 31 of row e >> 5,
+    // so each warp instruction reads one whole row; rows without a neighbour
+    // are zero-filled.  Issued before the MMAs: thread 0's warp stalls while
+    // the tensor pipe accepts them, and these copies are on every warp's path.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = tid + kEncThreads * i;
+      const int rr = e >> 5, cc = e & 31;
+      const int rj = sj[rr];
+      const float* src = p.NAC + (rj >= 0 ? (int64_t)rj * 256 + 128 + cc * 4 : 0);
+      cp_async16(X + rr * 512 + ((cc ^ (rr & 7)) << 4), src, rj >= 0);
+    }
+    cp_async_commit();
     if (tid == 0) {
       // each weight as hi + remainder: two MMAs into one accumulator
       uint32_t w = w_wait(j0, ok);
@@ -424,19 +438,6 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       mma_k128(tm, smem_u32(atile), w, 128, idesc, true);
       mma_commit(&bar_mma);
     }
-    // The tile rows' neighbour terms W11c h_j (512 B per row) into X while the
-    // D1 MMAs run: chunk e = tid + 512 i is 16-byte chunk e & 31 of row e >> 5,
-    // so each warp instruction reads one whole row; rows without a neighbour
-    // are zero-filled.
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int e = tid + kEncThreads * i;
-      const int rr = e >> 5, cc = e & 31;
-      const int rj = sj[rr];
-      const float* src = p.NAC + (rj >= 0 ? (int64_t)rj * 256 + 128 + cc * 4 : 0);
-      cp_async16(X + rr * 512 + ((cc ^ (rr & 7)) << 4), src, rj >= 0);
-    }
-    cp_async_commit();
     // this thread's slot; its own node term [W11a h_i + b11] (the slots of a
     // warp span at most two residues, so these loads are near-broadcasts)
     const int64_t s = t * 128 + row;
