@@ -81,19 +81,15 @@ __device__ __forceinline__ uint32_t idesc_f16(int M, int N) {
   return idesc_bf16(M, N) & ~((7u << 7) | (7u << 10));
 }
 
-// Copies `rows` rows of 128 fp16 (256 B) starting at global row `row0` into a
-// SW128 K-major tile of `tile_rows` rows; rows at or past `row_end` read as 0.
-__device__ __forceinline__ void load_rows_async(unsigned char* tile, const uint16_t* src,
-                                                int64_t row0, int64_t row_end, int tile_rows,
-                                                int tid) {
-  const int chunks = tile_rows * 16;
-  for (int c = tid; c < chunks; c += kEncThreads) {
-    const int r = c >> 4, k8 = c & 15;
-    const int64_t gr = row0 + r;
-    const bool ok = gr < row_end;
-    const uint16_t* p = src + (ok ? gr : 0) * kH + k8 * 8;
-    cp_async16(tile + sw128_offset(r, k8 * 8, tile_rows), p, ok);
-  }
+// h_E tile of `rows` rows from global row `row0` into the SW128 K-major tile
+// at `dst` (1024-byte aligned): two TMA boxes, one per 64-column atom; rows
+// past the end read as zero.  One thread issues it; `bar` completes when both
+// boxes have landed.
+__device__ __forceinline__ void tma_rows(unsigned char* dst, const CUtensorMap* map, int64_t row0,
+                                         int rows, uint64_t* bar) {
+  mbar_arrive_expect_tx(bar, (uint32_t)rows * 256u);
+  tma_load_2d(dst, map, 0, (int)row0, bar);
+  tma_load_2d(dst + rows * 128, map, 64, (int)row0, bar);
 }
 
 __device__ __forceinline__ void load_weights(unsigned char* dst, const unsigned char* const* imgs,
@@ -109,6 +105,7 @@ __device__ __forceinline__ void load_weights(unsigned char* dst, const unsigned 
 // ---------------------------------------------------------------------------
 constexpr int kNodeRes = 4;
 constexpr int kNodeSlots = kNodeRes * kK;                  // 192
+static_assert(kNodeSlots == kNodeTileRows, "node tile rows");
 constexpr uint32_t kNodeTileBytes = kNodeSlots * 256;      // 48 KiB
 constexpr uint32_t kNodeOffW = 0;                          // W1b, W2, W1b rem., W2 rem.
 constexpr uint32_t kNodeOffB = 4 * kW128Bytes;             // h_E tile
@@ -118,12 +115,12 @@ constexpr uint32_t kNodeSmem = kNodeOffJ + 2 * kNodeSlots * 4 + 1024;
 static_assert(kNodeSmem <= 227 * 1024, "node kernel shared memory");
 
 __global__ void __launch_bounds__(kEncThreads, 1)
-    enc_node_tc_kernel(EncNodeTcArgs p) {
+    enc_node_tc_kernel(const __grid_constant__ EncNodeTcArgs p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   int* SJ = reinterpret_cast<int*>(sm + kNodeOffJ);
   float* SA = reinterpret_cast<float*>(sm + kNodeOffJ + kNodeSlots * 4);
-  __shared__ uint64_t bar_w, bar_mma;
+  __shared__ uint64_t bar_w, bar_mma, bar_a;
   __shared__ uint32_t tmem_base;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -131,12 +128,12 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   const int f = quad * 32 + lane;
   const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
   const int R = p.bv.total_residues;
-  const int64_t SL = (int64_t)R * kK;
   const int tiles = (R + kNodeRes - 1) / kNodeRes;
 
   if (tid == 0) {
     mbar_init(&bar_w, 1);
     mbar_init(&bar_mma, 1);
+    mbar_init(&bar_a, 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -156,17 +153,21 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   uint32_t ph = 0;
   const float b2 = p.b2[f];
 
+  // h_E tiles arrive by TMA (thread 0 issues and waits; only the MMAs read them)
   int t = blockIdx.x;
-  if (t < tiles)
-    load_rows_async(sm + kNodeOffB, p.h_e, (int64_t)t * kNodeSlots, SL, kNodeSlots, tid);
-  cp_async_commit();
+  uint32_t ph_a = 0;
+  bool a_pending = false;   // thread 0: a tile load not yet waited for
+  if (tid == 0 && t < tiles) {
+    tma_rows(sm + kNodeOffB, &p.map_he, (int64_t)t * kNodeSlots, kNodeSlots, &bar_a);
+    a_pending = true;
+  }
   for (int it = 0; t < tiles; t += gridDim.x, ++it) {
     if (__syncthreads_or(!ok)) break;
     unsigned char* btile = sm + kNodeOffB;
-    cp_async_wait_all();
-    fence_async_smem();
-    __syncthreads();
     if (tid == 0) {
+      if (!mbar_wait(&bar_a, ph_a, p.err)) ok = false;
+      ph_a ^= 1;
+      a_pending = false;
       // D1 = W1b h_E as (hi + remainder) h_E: two MMAs into one accumulator
       tc_fence_after();
       mma_k128(tm, smem_u32(sm + kNodeOffW), smem_u32(btile), kNodeSlots,
@@ -213,9 +214,10 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     // The h_E tile is free once D1's MMAs have completed: the next tile's rows
     // load during this tile's epilogues.
     const int tn = t + gridDim.x;
-    if (tn < tiles)
-      load_rows_async(sm + kNodeOffB, p.h_e, (int64_t)tn * kNodeSlots, SL, kNodeSlots, tid);
-    cp_async_commit();
+    if (tid == 0 && tn < tiles) {
+      tma_rows(sm + kNodeOffB, &p.map_he, (int64_t)tn * kNodeSlots, kNodeSlots, &bar_a);
+      a_pending = true;
+    }
     // epilogue 1: G[slot][f] = GELU(D1 + N_i + N_j)  (16-bit stores, B layout),
     // 16 TMEM columns at a time
     unsigned char* G = sm + kNodeOffG;
@@ -282,7 +284,8 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     }
     tc_fence_before();
   }
-  cp_async_wait_all();
+  // no TMA load may be in flight when the CTA exits (after an early exit)
+  if (tid == 0 && a_pending) mbar_wait(&bar_a, ph_a, p.err);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -312,12 +315,12 @@ constexpr uint32_t kEdgeSmem = kEdgeOffX + 2 * kEdgeTileBytes + 1024;
 static_assert(kEdgeSmem <= 227 * 1024, "edge kernel shared memory");
 
 __global__ void __launch_bounds__(kEncThreads, 1)
-    enc_edge_tc_kernel(EncEdgeTcArgs p) {
+    enc_edge_tc_kernel(const __grid_constant__ EncEdgeTcArgs p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float (*red)[4][128] = reinterpret_cast<float (*)[4][128]>(sm + kEdgeOffRed);
   unsigned char* X = sm + kEdgeOffX;
-  __shared__ uint64_t bar_mma, bar_w[kEdgeRing];
+  __shared__ uint64_t bar_mma, bar_a, bar_w[kEdgeRing];
   // global residue row of each tile row's neighbour (-1: none); [it & 1] is
   // the current tile, the other buffer is filled for the next one
   __shared__ int SJ[2][128];
@@ -335,6 +338,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   int64_t t = blockIdx.x;
   if (tid == 0) {
     mbar_init(&bar_mma, 1);
+    mbar_init(&bar_a, 1);
     for (int i = 0; i < kEdgeRing; ++i) mbar_init(&bar_w[i], 1);
     fence_barrier_init();
   }
@@ -404,16 +408,18 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   // steps spread over the current tile so that no load is waited for
   int nx_e = -1, nx_b = 0, nx_L = 0, nx_off = 0;
 
-  if (t < tiles) load_rows_async(sm + kEdgeOffA, p.h_e, t * 128, SL, 128, tid);
-  cp_async_commit();
+  // h_E tiles arrive by TMA (thread 0 issues and waits; only the MMAs read them)
+  uint32_t ph_a = 0;
+  bool a_pending = false;   // thread 0: a tile load not yet waited for
+  if (tid == 0 && t < tiles) {
+    tma_rows(sm + kEdgeOffA, &p.map_he, t * 128, 128, &bar_a);
+    a_pending = true;
+  }
   for (int it = 0; t < tiles; t += gridDim.x, ++it) {
     if (__syncthreads_or(!ok)) break;
     const int j0 = 6 * it;
     const int* sj = SJ[it & 1];
     unsigned char* atile = sm + kEdgeOffA;
-    cp_async_wait_all();
-    fence_async_smem();
-    __syncthreads();
     // The tile rows' neighbour terms W11c h_j (512 B per row) into X while the
     // D1 MMAs run: chunk e = tid + 512 i is 16-byte chunk e & 31 of row e >> 5,
     // so each warp instruction reads one whole row; rows without a neighbour
@@ -429,6 +435,9 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     }
     cp_async_commit();
     if (tid == 0) {
+      if (!mbar_wait(&bar_a, ph_a, p.err)) ok = false;
+      ph_a ^= 1;
+      a_pending = false;
       // each weight as hi + remainder: two MMAs into one accumulator
       uint32_t w = w_wait(j0, ok);
       tc_fence_after();
@@ -472,15 +481,13 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       w_issue(j0 + 4);
     }
     const int64_t tn = t + gridDim.x;
-    {
-      if (tn < tiles) load_rows_async(atile, p.h_e, tn * 128, SL, 128, tid);
-      cp_async_commit();
+    if (tid == 0 && tn < tiles) {
+      tma_rows(atile, &p.map_he, tn * 128, 128, &bar_a);
+      a_pending = true;
       // The next tile's remainder rows into L2 a whole tile ahead of its
       // residual staging.
-      if (tid == 0 && tn < tiles) {
-        const int64_t rows = SL - tn * 128 < 128 ? SL - tn * 128 : 128;
-        bulk_prefetch_l2(p.h_e_lo + tn * 128 * kH, (uint32_t)(rows * kH * 2));
-      }
+      const int64_t rows = SL - tn * 128 < 128 ? SL - tn * 128 : 128;
+      bulk_prefetch_l2(p.h_e_lo + tn * 128 * kH, (uint32_t)(rows * kH * 2));
     }
     if (tid < 128) {   // next tile's index chain, step 1
       nx_e = -1;
@@ -567,7 +574,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
         *reinterpret_cast<uint4*>(G + sw128_offset(row, c0 + 8 * u, 128)) =
             make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
     }
-    cp_async_wait_all();   // residual rows (and the next tile's h_E rows)
+    cp_async_wait_all();   // residual rows
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -688,11 +695,13 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     tc_fence_before();
   }
   cp_async_wait_all();
-  // Drain: no bulk copy may be in flight when the CTA exits (entries issued
-  // but not waited for after an early exit).
-  if (tid == 0)
+  // Drain: no bulk or TMA copy may be in flight when the CTA exits (entries
+  // issued but not waited for after an early exit).
+  if (tid == 0) {
     for (int j = w_landed; j < w_issued; ++j)
       mbar_wait(&bar_w[j % kEdgeRing], (uint32_t)((j / kEdgeRing) & 1), p.err);
+    if (a_pending) mbar_wait(&bar_a, ph_a, p.err);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -985,13 +994,20 @@ __global__ void __launch_bounds__(kEncThreads, 1)
 // ---------------------------------------------------------------------------
 constexpr uint32_t kTabOffW = 0;                            // 3 images
 constexpr uint32_t kTabOffA = 3 * kW128Bytes;               // 2 h_E tiles
-constexpr uint32_t kTabSmem = kTabOffA + 2 * kEdgeTileBytes + 1024;
+// X: one layer's gathered PVenc rows [128][256 B], then that layer's output
+// rows [128][256 B] (16-bit), so that gathers and stores move whole rows
+constexpr uint32_t kTabOffX = kTabOffA + 2 * kEdgeTileBytes;
+constexpr uint32_t kTabSmem = kTabOffX + 2 * kEdgeTileBytes + 1024;
+static_assert(kTabSmem <= 227 * 1024, "table kernel shared memory");
 
-__global__ void __launch_bounds__(kEncThreads, 1) dec_tables_tc_kernel(DecTablesTcArgs p) {
+__global__ void __launch_bounds__(kEncThreads, 1)
+    dec_tables_tc_kernel(const __grid_constant__ DecTablesTcArgs p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  __shared__ uint64_t bar_w, bar_mma;
+  __shared__ uint64_t bar_w, bar_mma, bar_a[2];
+  __shared__ int SJ[128];   // global residue row of each tile row's neighbour (-1: none)
   __shared__ uint32_t tmem_base;
+  unsigned char* X = sm + kTabOffX;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, cg = warp >> 2;
@@ -1004,6 +1020,8 @@ __global__ void __launch_bounds__(kEncThreads, 1) dec_tables_tc_kernel(DecTables
   if (tid == 0) {
     mbar_init(&bar_w, 1);
     mbar_init(&bar_mma, 1);
+    mbar_init(&bar_a[0], 1);
+    mbar_init(&bar_a[1], 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -1023,69 +1041,113 @@ __global__ void __launch_bounds__(kEncThreads, 1) dec_tables_tc_kernel(DecTables
   uint32_t ph = 0;
   const uint32_t idesc = idesc_f16(128, 128);
 
+  // h_E tiles arrive by TMA into two buffers, one tile ahead (thread 0 issues
+  // and waits; only the MMAs read them)
   int64_t t = blockIdx.x;
-  if (t < tiles) load_rows_async(sm + kTabOffA, p.h_e, t * 128, SL, 128, tid);
-  cp_async_commit();
+  uint32_t ph_a = 0;     // bit b: phase parity of bar_a[b]
+  int a_pending = 0;     // bit b: a load into buffer b not yet waited for
+  if (tid == 0 && t < tiles) {
+    tma_rows(sm + kTabOffA, &p.map_he, t * 128, 128, &bar_a[0]);
+    a_pending = 1;
+  }
   for (int it = 0; t < tiles; t += gridDim.x, ++it) {
     if (__syncthreads_or(!ok)) break;
     const int buf = it & 1;
     unsigned char* atile = sm + kTabOffA + buf * kEdgeTileBytes;
-    cp_async_wait_all();
-    fence_async_smem();
-    __syncthreads();
+    const int64_t tn = t + gridDim.x;
     if (tid == 0) {
+      // next tile into the other buffer (its MMAs completed last iteration)
+      if (tn < tiles) {
+        tma_rows(sm + kTabOffA + (buf ^ 1) * kEdgeTileBytes, &p.map_he, tn * 128, 128,
+                 &bar_a[buf ^ 1]);
+        a_pending |= 1 << (buf ^ 1);
+      }
+      if (!mbar_wait(&bar_a[buf], (ph_a >> buf) & 1u, p.err)) ok = false;
+      ph_a ^= 1u << buf;
+      a_pending &= ~(1 << buf);
       tc_fence_after();
       for (int l = 0; l < 3; ++l)
         mma_k128(tm + 128u * l, smem_u32(atile), smem_u32(sm + kTabOffW + l * kW128Bytes), 128,
                  idesc, false);
       mma_commit(&bar_mma);
     }
-    // next tile into the other buffer (its MMAs completed last iteration)
-    const int64_t tn = t + gridDim.x;
-    if (tn < tiles)
-      load_rows_async(sm + kTabOffA + (buf ^ 1) * kEdgeTileBytes, p.h_e, tn * 128, SL, 128, tid);
-    cp_async_commit();
-    // this thread's slot and its neighbour's residue row (-1: no neighbour)
-    const int64_t s = t * 128 + row;
-    int rj = -1;
-    if (s < SL) {
-      const int r = (int)(s / kK), k = (int)(s % kK);
-      const int b = p.bv.res_prot[r];
-      const int L = p.bv.prot_len[b];
-      const int j = k < (L < kK ? L : kK) ? p.e_idx[s] : -1;
-      if (j >= 0 && j < L) rj = p.bv.prot_res_off[b] + j;
+    // neighbour residue row of each tile row (-1: no neighbour)
+    if (tid < 128) {
+      const int64_t s = t * 128 + tid;
+      int rj = -1;
+      if (s < SL) {
+        const int r = (int)(s / kK), k = (int)(s % kK);
+        const int b = p.bv.res_prot[r];
+        const int L = p.bv.prot_len[b];
+        const int j = k < (L < kK ? L : kK) ? p.e_idx[s] : -1;
+        if (j >= 0 && j < L) rj = p.bv.prot_res_off[b] + j;
+      }
+      SJ[tid] = rj;
     }
-    uint4 pv[3][4];   // the three layers' PVenc rows, in flight during the MMA wait
+    __syncthreads();
+    // layer l's PVenc rows of the tile's neighbours into X[0, 32 KiB): chunk
+    // e = tid + 512 i is 16-byte chunk e & 15 of row e >> 4, so a warp
+    // instruction reads two whole rows; rows without a neighbour are zero
+    auto stage_pv = [&](int l) {
 #pragma unroll
-    for (int l = 0; l < 3; ++l)
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        pv[l][u] = rj >= 0 ? ld_nc_noalloc_v4(p.PVenc[l] + (int64_t)rj * kH + c0 + 8 * u)
-                           : make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < 4; ++i) {
+        const int e = tid + kEncThreads * i;
+        const int rr = e >> 4, cc = e & 15;
+        const int rj = SJ[rr];
+        const uint16_t* src = p.PVenc[l] + (rj >= 0 ? (int64_t)rj * kH + cc * 8 : 0);
+        cp_async16(X + rr * 256 + ((cc ^ (rr & 15)) << 4), src, rj >= 0);
+      }
+      cp_async_commit();
+    };
+    stage_pv(0);
     if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
     ph ^= 1;
     tc_fence_after();
-#pragma unroll
     for (int l = 0; l < 3; ++l) {
-      float v[32];
-      tmem_ld32(tm + lane_base + 128u * l + (uint32_t)c0, v);
-      if (s < SL) {
+      cp_async_wait_all();
+      __syncthreads();   // layer l's rows landed; layer l-1's copy-out is done
+      {
+        float v[32];
+        tmem_ld32(tm + lane_base + 128u * l + (uint32_t)c0, v);
         uint32_t pk[16];
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const uint32_t w = (&pv[l][q >> 2].x)[q & 3];
-          const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&w));
-          pk[q] = pack_h2(v[2 * q] + e.x, v[2 * q + 1] + e.y);
-        }
-        uint4* dst = reinterpret_cast<uint4*>(p.out[l] + s * kH + c0);
+        for (int u = 0; u < 4; ++u) {
+          const int co = ((cg * 4 + u) ^ (row & 15)) << 4;
+          const uint4 ev = *reinterpret_cast<const uint4*>(X + row * 256 + co);
+          const uint32_t ew[4] = {ev.x, ev.y, ev.z, ev.w};
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+          for (int i = 0; i < 4; ++i) {
+            const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&ew[i]));
+            const int q = 4 * u + i;
+            pk[q] = pack_h2(v[2 * q] + e.x, v[2 * q + 1] + e.y);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int co = ((cg * 4 + u) ^ (row & 15)) << 4;
+          *reinterpret_cast<uint4*>(X + kEdgeTileBytes + row * 256 + co) =
+              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+      }
+      __syncthreads();   // every PVenc read of layer l and every output write are done
+      if (l < 2) stage_pv(l + 1);
+      // layer l's table rows, copied out as whole rows
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int e = tid + kEncThreads * i;
+        const int rr = e >> 4, cc = e & 15;
+        const int64_t so = t * 128 + rr;
+        if (so < SL)
+          *reinterpret_cast<uint4*>(p.out[l] + so * kH + cc * 8) = *reinterpret_cast<const uint4*>(
+              X + kEdgeTileBytes + rr * 256 + ((cc ^ (rr & 15)) << 4));
       }
     }
     tc_fence_before();
   }
-  cp_async_wait_all();
+  // no TMA load may be in flight when the CTA exits (after an early exit)
+  if (tid == 0)
+    for (int b = 0; b < 2; ++b)
+      if ((a_pending >> b) & 1) mbar_wait(&bar_a[b], (ph_a >> b) & 1u, p.err);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -1093,6 +1155,40 @@ __global__ void __launch_bounds__(kEncThreads, 1) dec_tables_tc_kernel(DecTables
 }
 
 }  // namespace
+
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// The driver's cuTensorMapEncodeTiled, looked up once through the runtime (no
+// link against libcuda).
+EncodeTiledFn encode_tiled() {
+  static const EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (EncodeTiledFn) nullptr;
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+}  // namespace
+
+bool make_rows_tensor_map(CUtensorMap* map, const uint16_t* base, int64_t rows, int box_rows) {
+  const EncodeTiledFn fn = encode_tiled();
+  if (!fn || !base || rows <= 0 || rows > 0x7FFFFFFF || box_rows <= 0 || box_rows > 256) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)kH, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kH * 2};   // bytes between rows
+  const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};  // 64 fp16 = one 128-byte swizzle span
+  const cuuint32_t estride[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(base), dims, strides,
+            box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 void launch_enc_node_tc(cudaStream_t st, const EncNodeTcArgs& p, int num_sms) {
   const int tiles = (p.bv.total_residues + kNodeRes - 1) / kNodeRes;

@@ -851,12 +851,18 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   e->launches += 2;
   HKB_CUDA(cudaMemsetAsync(eo->h_v, 0, sizeof(float) * R * kH, st));
   e->launches += 1;
+  // TMA tensor maps of h_E (value) for the node and edge passes' tile loads
+  CUtensorMap map_node, map_edge;
+  if (!make_rows_tensor_map(&map_node, eo->h_e16, SL, kNodeTileRows) ||
+      !make_rows_tensor_map(&map_edge, eo->h_e16, SL, 128))
+    return internal("TMA tensor map encoding failed");
   for (int l = 0; l < 3; ++l) {
     const auto& E = w.enc[l];
     const std::string q = "enc" + std::to_string(l) + ".";
     // node messages: one fused pass over h_E (W1b, gathers, GELU, W2, GELU, slot sum)
     lin(256, kH, eo->h_v, kH, q + "nW1ac", E.b1ac, 0, NAC, 256);
     EncNodeTcArgs na;
+    na.map_he = map_node;
     na.bv = bv;
     na.h_e = eo->h_e16;
     na.e_idx = eo->e_idx;
@@ -879,6 +885,7 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
     // edge update: one fused pass (W11b, gathers, GELU, W12, GELU, W13, LN3)
     lin(256, kH, eo->h_v, kH, q + "nW11ac", E.b11ac, 0, NAC, 256);
     EncEdgeTcArgs ea;
+    ea.map_he = map_edge;
     ea.bv = bv;
     ea.h_e = eo->h_e16;
     ea.h_e_out = eo->h_e16;
@@ -910,6 +917,8 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const BatchView
   cudaStream_t st = e->stream;
   const int64_t R = hb.R, SL = R * kK;
   DecTablesTcArgs ta;
+  if (with_pe && !make_rows_tensor_map(&ta.map_he, eo.h_e16, SL, 128))
+    return internal("TMA tensor map encoding failed");
   ta.bv = db_bv;
   ta.e_idx = eo.e_idx;
   ta.h_e = eo.h_e16;

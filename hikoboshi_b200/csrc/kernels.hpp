@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace hkb {
@@ -241,7 +242,15 @@ struct ArBf16Args {
 
 // Fused encoder-layer kernels (tensor-core modes; h_E fp16 [R*48,128]).
 // NAC = [W1a h + b1 | W1c h] per residue, fp32 [R,256].
+// Tensor map of a row-major [rows, 128] fp16 array (h_E) for 2-D TMA loads of
+// [box_rows, 64] boxes with the 128-byte swizzle: one box lands as one
+// 64-column atom of the SW128 K-major operand layout.  False if the driver
+// cannot encode it.
+bool make_rows_tensor_map(CUtensorMap* map, const uint16_t* base, int64_t rows, int box_rows);
+constexpr int kNodeTileRows = 192;   // enc_node_tc: 4 residues x 48 slots per tile
+
 struct EncNodeTcArgs {
+  alignas(64) CUtensorMap map_he;       // h_E value, boxes of kNodeTileRows rows
   BatchView bv;
   const uint16_t* h_e = nullptr;
   const int* e_idx = nullptr;
@@ -259,6 +268,7 @@ struct EncNodeTcArgs {
 void launch_enc_node_tc(cudaStream_t st, const EncNodeTcArgs& p, int num_sms);
 
 struct EncEdgeTcArgs {
+  alignas(64) CUtensorMap map_he;       // h_E value, boxes of 128 rows
   BatchView bv;
   const uint16_t* h_e = nullptr;        // read
   uint16_t* h_e_out = nullptr;          // written on slots with a valid neighbour (may alias)
@@ -308,6 +318,7 @@ void launch_enc_featurize_tc(cudaStream_t st, const EncFeatTcArgs& p, int num_sm
 // 0) reads only this row; a decoded neighbour adds the 16-bit correction
 // W1d_l h_j - PVenc_l[j] that the decode kernel stores when it decodes j.
 struct DecTablesTcArgs {
+  alignas(64) CUtensorMap map_he;        // h_E value, boxes of 128 rows
   BatchView bv;
   const int* e_idx = nullptr;            // [R,48]
   const uint16_t* h_e = nullptr;

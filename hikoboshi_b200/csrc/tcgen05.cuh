@@ -16,6 +16,7 @@
 // major bits 15/16, N >> 3 at 17-22, M >> 4 at 24-28).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -121,6 +122,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
           "r"(smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---- tiled TMA load (tensor map, no multicast) -------------------------------
+// Copies the box at element coordinates (x, y) of the 2-D tensor `map` (x the
+// innermost coordinate) into shared memory at `dst` and completes its bytes on
+// `bar`.  Boxes with the 128-byte swizzle need a 1024-byte aligned `dst`, and
+// x * element size must be a multiple of 16 bytes; rows past the tensor's
+// extent read as zero.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
 
