@@ -479,16 +479,25 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           const int code = Nb[s][k];
           const bool bw = (code >> 16) & 1;
           const int tok = code >> 17;
-          float pe[8], pv[8];
+          float pe[8];
           unpack8<F16>(pe_raw[i], pe);
-          unpack8<F16>(v_raw[i], pv);
-          float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+          float2 t2[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) t2[q] = make_float2(pe[2 * q], pe[2 * q + 1]);
           if (bw) {
+            // decoded neighbour: (table + correction) + W1c W_s[tok]; the
+            // correction row is zero at layer 0 and for undecoded neighbours,
+            // which skip both terms (the sums are the same)
+            float pv[8];
+            unpack8<F16>(v_raw[i], pv);
             const float4* st = reinterpret_cast<const float4*>(StabL + tok * kH) + c8 * 2;
-            s0 = st[0];
-            s1 = st[1];
+            const float4 s0 = st[0], s1 = st[1];
+            const float st8[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              t2[q] = __fadd2_rn(__fadd2_rn(t2[q], make_float2(pv[2 * q], pv[2 * q + 1])),
+                                 make_float2(st8[2 * q], st8[2 * q + 1]));
           }
-          const float st8[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
           const float4 a0 =
               kChunkSeqs == 1 ? ca0 : reinterpret_cast<const float4*>(Aa[s])[c8 * 2];
           const float4 a1 =
@@ -498,12 +507,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) ar_decode_tc_kernel(
           // b2 (W2 is linear and a power-of-two scale is exact)
           float2 y[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 t2 = __fadd2_rn(__fadd2_rn(make_float2(pe[2 * q], pe[2 * q + 1]),
-                                                    make_float2(pv[2 * q], pv[2 * q + 1])),
-                                         make_float2(st8[2 * q], st8[2 * q + 1]));
-            y[q] = gelu2_tc_x2(__fadd2_rn(make_float2(av[2 * q], av[2 * q + 1]), t2));
-          }
+          for (int q = 0; q < 4; ++q)
+            y[q] = gelu2_tc_x2(__fadd2_rn(make_float2(av[2 * q], av[2 * q + 1]), t2[q]));
           outv = make_uint4(pack16<F16>(y[0].x, y[0].y), pack16<F16>(y[1].x, y[1].y),
                             pack16<F16>(y[2].x, y[2].y), pack16<F16>(y[3].x, y[3].y));
         }
