@@ -712,10 +712,11 @@ __global__ void __launch_bounds__(kEncThreads, 1)
 // Featurisation kernel: 128 slots per tile (inverse_fold_scalar.cpp:236-279,
 // edge_rbf_features_scalar.cpp:45-137):
 //   f   = [W_pos[:, class(i - j)] + b_pos (16) | RBF of 25 atom pairs (400) | 0 (32)]
-//   E   = f W_edge^T          K = 448 as two chunks of 4 and 3 64-column atoms
+//   E   = f W_edge^T          K = 448 as four chunks of 2, 2, 2 and 1 64-column atoms
 //   h_E = LN_e(E) W_e^T + b_e   (fp16 out)
-// Features are computed straight into the SW128 operand (fp16), so the
-// [R*48, 416] feature matrix never exists in HBM.
+// Features are computed straight into the SW128 operand, each once, as fp16
+// value and fp16 remainder, so the [R*48, 416] feature matrix never exists
+// in HBM.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kAtomBytes = 128 * 128;                    // 128 rows x 64 fp16
 constexpr uint32_t kFeatOffWedge = 0;                         // 7 atoms
@@ -725,12 +726,13 @@ constexpr uint32_t kFeatOffRow = kFeatOffA + 4 * kAtomBytes;  // int [3][128]
 constexpr uint32_t kFeatOffRed = kFeatOffRow + 3 * 128 * 4;   // float [2][4][128]
 constexpr uint32_t kFeatSmem = kFeatOffRed + 2 * 4 * 128 * 4 + 1024;
 
-// One RBF item: the 16 values of atom pair p for tile row `row`, as two
-// 16-byte chunks at local column `col` of the feature chunk.
+// One RBF item: the 16 values of atom pair p for tile row `row`, computed
+// once and stored as fp16 values at local column `col` of the K chunk
+// (operand atoms 0-1) and as fp16 remainders at `col` + 128 (atoms 2-3).
 __device__ __forceinline__ void feat_pair_item(unsigned char* A, int row, int p, int col,
                                                const int* SR, const int* SJ,
-                                               const EncFeatTcArgs& a, bool lo) {
-  uint32_t pk[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                                               const EncFeatTcArgs& a) {
+  uint32_t ph[8] = {0, 0, 0, 0, 0, 0, 0, 0}, pl[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   const int r = SR[row], rj = SJ[row];
   if (rj >= 0) {
     const int ai = c_pairs[p][0], aj = c_pairs[p][1];
@@ -738,13 +740,20 @@ __device__ __forceinline__ void feat_pair_item(unsigned char* A, int row, int p,
       const float dist =
           pair_distance(a.coords + ((int64_t)r * 5 + ai) * 3, a.coords + ((int64_t)rj * 5 + aj) * 3);
 #pragma unroll
-      for (int f = 0; f < 8; ++f)
-        pk[f] = pack_h2s(rbf_fast(dist, 2 * f), rbf_fast(dist, 2 * f + 1), lo);
+      for (int f = 0; f < 8; ++f) {
+        const float x0 = rbf_fast(dist, 2 * f), x1 = rbf_fast(dist, 2 * f + 1);
+        ph[f] = pack_h2s(x0, x1, false);
+        pl[f] = pack_h2s(x0, x1, true);
+      }
     }
   }
-  *reinterpret_cast<uint4*>(A + sw128_offset(row, col, 128)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  *reinterpret_cast<uint4*>(A + sw128_offset(row, col, 128)) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
   *reinterpret_cast<uint4*>(A + sw128_offset(row, col + 8, 128)) =
-      make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      make_uint4(ph[4], ph[5], ph[6], ph[7]);
+  *reinterpret_cast<uint4*>(A + sw128_offset(row, col + 128, 128)) =
+      make_uint4(pl[0], pl[1], pl[2], pl[3]);
+  *reinterpret_cast<uint4*>(A + sw128_offset(row, col + 136, 128)) =
+      make_uint4(pl[4], pl[5], pl[6], pl[7]);
 }
 
 __global__ void __launch_bounds__(kEncThreads, 1)
@@ -818,56 +827,42 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       SC[tid] = cls;
     }
     __syncthreads();
-    // chunk 1: positional block (columns 0-15) and pairs 0-14 (16-255), as
-    // fp16 values (pass 0) and then their fp16 remainders (pass 1), each
-    // pass followed by its MMAs into the same accumulator
-    for (int pass = 0; pass < 2; ++pass) {
-      const bool lo = pass == 1;
-      for (int m = tid; m < 256 + 15 * 128; m += kEncThreads) {
-        if (m < 256) {
+    // The 448 feature columns (positional block 0-15, pairs 0-24 at 16-415,
+    // zeros 416-447) in four K chunks of 128, 128, 128 and 64 columns
+    // (pairs 0-6, 7-14, 15-22, 23-24).  Each feature is computed once and
+    // stored as its fp16 value (operand atoms 0-1) and fp16 remainder (atoms
+    // 2-3); the chunk's value and remainder products accumulate into E.
+    for (int c = 0; c < 4; ++c) {
+      const int p0 = c == 0 ? 0 : 8 * c - 1;           // first pair of the chunk
+      const int np = c == 0 ? 7 : (c == 3 ? 2 : 8);    // pairs in the chunk
+      const int npos = c == 0 ? 256 : 0;               // 128 rows x 2 positional halves
+      const int nzero = c == 3 ? 4 * 128 : 0;          // 128 rows x 4 zero 8-column parts
+      const int items = npos + np * 128 + nzero;
+      for (int m = tid; m < items; m += kEncThreads) {
+        if (m < npos) {
           const int rw = m >> 1, h = (m & 1) * 8;
           const int cls = SC[rw];
-          uint32_t pk[4] = {0, 0, 0, 0};
+          uint32_t vh[4] = {0, 0, 0, 0}, vl[4] = {0, 0, 0, 0};
           if (cls >= 0) {
 #pragma unroll
             for (int d = 0; d < 4; ++d) {
               const int d0 = h + 2 * d;
-              pk[d] = pack_h2s(p.pos_w[d0 * kPosClasses + cls] + p.pos_b[d0],
-                               p.pos_w[(d0 + 1) * kPosClasses + cls] + p.pos_b[d0 + 1], lo);
+              const float x0 = p.pos_w[d0 * kPosClasses + cls] + p.pos_b[d0];
+              const float x1 = p.pos_w[(d0 + 1) * kPosClasses + cls] + p.pos_b[d0 + 1];
+              vh[d] = pack_h2s(x0, x1, false);
+              vl[d] = pack_h2s(x0, x1, true);
             }
           }
           *reinterpret_cast<uint4*>(A + sw128_offset(rw, h, 128)) =
-              make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              make_uint4(vh[0], vh[1], vh[2], vh[3]);
+          *reinterpret_cast<uint4*>(A + sw128_offset(rw, h + 128, 128)) =
+              make_uint4(vl[0], vl[1], vl[2], vl[3]);
+        } else if (m < npos + np * 128) {
+          const int q = m - npos, rw = q & 127, pr = p0 + (q >> 7);
+          feat_pair_item(A, rw, pr, 16 + 16 * pr - 128 * c, SR, SJ, p);
         } else {
-          const int q = m - 256, rw = q & 127, pr = q >> 7;
-          feat_pair_item(A, rw, pr, 16 + 16 * pr, SR, SJ, p, lo);
-        }
-      }
-      fence_async_smem();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        for (int kk = 0; kk < 16; ++kk) {
-          const uint32_t o = (uint32_t)(kk >> 2) * kAtomBytes + (uint32_t)(kk & 3) * 32u;
-          mma_bf16(tm, sw128_desc(smem_u32(A) + o), sw128_desc(smem_u32(sm + kFeatOffWedge) + o),
-                   idesc, (kk > 0 || lo) ? 1u : 0u);
-        }
-        mma_commit(&bar_mma);
-      }
-      if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
-      ph ^= 1;
-      tc_fence_after();
-    }
-    // chunk 2: pairs 15-24 (columns 256-415) and zero padding (416-447), the
-    // same two passes
-    for (int pass = 0; pass < 2; ++pass) {
-      const bool lo = pass == 1;
-      for (int m = tid; m < 10 * 128 + 4 * 128; m += kEncThreads) {
-        if (m < 10 * 128) {
-          const int rw = m & 127, pr = 15 + (m >> 7);
-          feat_pair_item(A, rw, pr, 16 + 16 * pr - 256, SR, SJ, p, lo);
-        } else {
-          const int q = m - 10 * 128, rw = q >> 2, u = q & 3;
+          const int q = m - npos - np * 128, rw = q >> 2, u = q & 3;
+          *reinterpret_cast<uint4*>(A + sw128_offset(rw, 32 + 8 * u, 128)) = make_uint4(0, 0, 0, 0);
           *reinterpret_cast<uint4*>(A + sw128_offset(rw, 160 + 8 * u, 128)) = make_uint4(0, 0, 0, 0);
         }
       }
@@ -875,11 +870,14 @@ __global__ void __launch_bounds__(kEncThreads, 1)
       __syncthreads();
       if (tid == 0) {
         tc_fence_after();
-        for (int kk = 0; kk < 12; ++kk) {
-          const uint32_t o = (uint32_t)(kk >> 2) * kAtomBytes + (uint32_t)(kk & 3) * 32u;
-          mma_bf16(tm, sw128_desc(smem_u32(A) + o),
-                   sw128_desc(smem_u32(sm + kFeatOffWedge) + 4 * kAtomBytes + o), idesc, 1u);
-        }
+        const uint32_t wb = smem_u32(sm + kFeatOffWedge) + (uint32_t)(2 * c) * kAtomBytes;
+        const int ksteps = c == 3 ? 4 : 8;
+        for (int half = 0; half < 2; ++half)
+          for (int kk = 0; kk < ksteps; ++kk) {
+            const uint32_t o = (uint32_t)(kk >> 2) * kAtomBytes + (uint32_t)(kk & 3) * 32u;
+            mma_bf16(tm, sw128_desc(smem_u32(A) + (uint32_t)half * 2u * kAtomBytes + o),
+                     sw128_desc(wb + o), idesc, (c > 0 || half > 0 || kk > 0) ? 1u : 0u);
+          }
         mma_commit(&bar_mma);
       }
       if (!mbar_wait(&bar_mma, ph, p.err)) ok = false;
