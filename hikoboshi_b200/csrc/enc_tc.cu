@@ -153,18 +153,22 @@ __global__ void __launch_bounds__(kEncThreads, 1)
   uint32_t ph = 0;
   const float b2 = p.b2[f];
 
-  // h_E tiles arrive by TMA (thread 0 issues and waits; only the MMAs read them)
+  // h_E tiles arrive by TMA; thread kIssuer issues them and the tile's MMAs.
+  // It sits outside the threads that fill SJ / SA, so its stall while the
+  // tensor pipe accepts the MMAs overlaps their index loads.
+  constexpr int kIssuer = kEncThreads - 64;
+  static_assert(kIssuer >= kNodeSlots, "MMA issuer outside the SJ / SA threads");
   int t = blockIdx.x;
   uint32_t ph_a = 0;
-  bool a_pending = false;   // thread 0: a tile load not yet waited for
-  if (tid == 0 && t < tiles) {
+  bool a_pending = false;   // kIssuer: a tile load not yet waited for
+  if (tid == kIssuer && t < tiles) {
     tma_rows(sm + kNodeOffB, &p.map_he, (int64_t)t * kNodeSlots, kNodeSlots, &bar_a);
     a_pending = true;
   }
   for (int it = 0; t < tiles; t += gridDim.x, ++it) {
     if (__syncthreads_or(!ok)) break;
     unsigned char* btile = sm + kNodeOffB;
-    if (tid == 0) {
+    if (tid == kIssuer) {
       if (!mbar_wait(&bar_a, ph_a, p.err)) ok = false;
       ph_a ^= 1;
       a_pending = false;
@@ -214,7 +218,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     // The h_E tile is free once D1's MMAs have completed: the next tile's rows
     // load during this tile's epilogues.
     const int tn = t + gridDim.x;
-    if (tid == 0 && tn < tiles) {
+    if (tid == kIssuer && tn < tiles) {
       tma_rows(sm + kNodeOffB, &p.map_he, (int64_t)tn * kNodeSlots, kNodeSlots, &bar_a);
       a_pending = true;
     }
@@ -244,7 +248,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == kIssuer) {
       tc_fence_after();
       mma_k128(tm, smem_u32(sm + kNodeOffW + kW128Bytes), smem_u32(G), kNodeSlots,
                idesc_f16(128, kNodeSlots), false);
@@ -285,7 +289,7 @@ __global__ void __launch_bounds__(kEncThreads, 1)
     tc_fence_before();
   }
   // no TMA load may be in flight when the CTA exits (after an early exit)
-  if (tid == 0 && a_pending) mbar_wait(&bar_a, ph_a, p.err);
+  if (tid == kIssuer && a_pending) mbar_wait(&bar_a, ph_a, p.err);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
