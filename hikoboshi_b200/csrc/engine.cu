@@ -808,7 +808,11 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   eo->d2 = ws.get_as<float>("e.d2", SL);
   eo->mask = ws.get_as<float>("e.mask", R);
   eo->h_e = nullptr;
-  eo->h_e16 = ws.get_as<uint16_t>("e.he16", SL * kH);
+  // h_E (value) holds at least one TMA box of rows (kNodeTileRows), so the
+  // tensor maps of the encoder passes never describe fewer rows than a box;
+  // rows past SL are zero
+  eo->h_e_rows = SL < kNodeTileRows ? (int64_t)kNodeTileRows : SL;
+  eo->h_e16 = ws.get_as<uint16_t>("e.he16", eo->h_e_rows * kH);
   eo->h_e16lo = ws.get_as<uint16_t>("e.he16lo", SL * kH);
   eo->h_v = ws.get_as<float>("e.hv", R * kH);
   float* NAC = ws.get_as<float>("e.nac", R * 256);
@@ -852,9 +856,12 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   HKB_CUDA(cudaMemsetAsync(eo->h_v, 0, sizeof(float) * R * kH, st));
   e->launches += 1;
   // TMA tensor maps of h_E (value) for the node and edge passes' tile loads
+  if (eo->h_e_rows > SL)
+    HKB_CUDA(cudaMemsetAsync(eo->h_e16 + SL * kH, 0,
+                             sizeof(uint16_t) * (size_t)(eo->h_e_rows - SL) * kH, st));
   CUtensorMap map_node, map_edge;
-  if (!make_rows_tensor_map(&map_node, eo->h_e16, SL, kNodeTileRows) ||
-      !make_rows_tensor_map(&map_edge, eo->h_e16, SL, 128))
+  if (!make_rows_tensor_map(&map_node, eo->h_e16, eo->h_e_rows, kNodeTileRows) ||
+      !make_rows_tensor_map(&map_edge, eo->h_e16, eo->h_e_rows, 128))
     return internal("TMA tensor map encoding failed");
   for (int l = 0; l < 3; ++l) {
     const auto& E = w.enc[l];
@@ -917,7 +924,7 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const BatchView
   cudaStream_t st = e->stream;
   const int64_t R = hb.R, SL = R * kK;
   DecTablesTcArgs ta;
-  if (with_pe && !make_rows_tensor_map(&ta.map_he, eo.h_e16, SL, 128))
+  if (with_pe && !make_rows_tensor_map(&ta.map_he, eo.h_e16, eo.h_e_rows, 128))
     return internal("TMA tensor map encoding failed");
   ta.bv = db_bv;
   ta.e_idx = eo.e_idx;

@@ -66,8 +66,9 @@ struct EncoderOut {
   float* d2 = nullptr;    // [R,48]
   float* mask = nullptr;  // [R]
   float* h_e = nullptr;   // [R,48,128] (fp32 encoder)
-  uint16_t* h_e16 = nullptr;  // [R,48,128] fp16 (tensor-core encoder)
-  uint16_t* h_e16lo = nullptr;  // its fp16 remainder (h_E = hi + lo)
+  uint16_t* h_e16 = nullptr;  // [h_e_rows,128] fp16 (tensor-core encoder); rows past R*48 are 0
+  uint16_t* h_e16lo = nullptr;  // [R*48,128] its fp16 remainder (h_E = hi + lo)
+  int64_t h_e_rows = 0;         // rows of h_e16: max(R*48, one TMA box of the encoder passes)
   float* h_v = nullptr;   // [R,128]
 };
 

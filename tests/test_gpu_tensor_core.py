@@ -66,6 +66,23 @@ def test_tensor_core_design_matches_oracle(request, oracle, precision, tol):
         assert (again.log_probs[b] == res.log_probs[b]).all()
 
 
+def test_f16_single_tiny_proteins(engine_f16, oracle):
+    """One protein of 1, 2 or 3 residues per call: the edge tensor then has
+    fewer rows (48 L) than one TMA box of the encoder passes (128 or 192
+    rows), whose rows past the end read as zero.  Design and teacher-forced
+    scoring both run and match the oracle within the 16-bit bar."""
+    from hikoboshi_b200 import synthetic_backbone
+    for L in (1, 2, 3):
+        c, s = synthetic_backbone(900 + L, L)
+        res = engine_f16.design([c], [s], num_seqs=2, seeds=5, temperatures=0.1)
+        for q in range(2):
+            check_design(oracle, c, s, res.tokens[0][q], res.log_probs[0][q], res.orders[0][q],
+                         5 + q, 0.1, 2e-2 / 0.1)
+        toks = res.tokens[0][:1].astype(np.int32)
+        lp, _, sc = engine_f16.score([c], [s], [toks], seeds=5)[0]
+        assert lp.shape == (1, L, 21) and np.isfinite(lp).all() and np.isfinite(sc).all()
+
+
 def test_f16_full_size_properties(engine_f16, engine_fp32, oracle):
     """Config-2 sized batch (64 x L=256 x 32): properties that hold at any
     size -- valid tokens, each emitted row a normalised distribution,
