@@ -28,10 +28,11 @@
 // All are persistent (one CTA per SM, 16 warps).  Weight images arrive by bulk
 // copies: the node pass and the featurisation keep theirs resident, the edge
 // pass streams its six images through a 3-slot ring and uses the space to
-// stage its row gathers.  The next tile's h_E rows are fetched by cp.async as
-// soon as the current tile's first MMA has read them, node terms are gathered
-// while MMAs run, and a tile's MMAs are issued by thread 0 and
-// completion-tracked on one mbarrier.  Every wait is bounded.
+// stage its row gathers.  The next tile's h_E rows are fetched by TMA (a 2-D
+// tensor map over this GPU's own h_E, 128-byte swizzle, no multicast) as soon
+// as the current tile's first MMA has read them, node terms are gathered while
+// MMAs run, and a tile's MMAs are issued by one thread and completion-tracked
+// on one mbarrier.  Every wait is bounded.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
