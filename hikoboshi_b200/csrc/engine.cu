@@ -852,9 +852,8 @@ hkb_status encode_tc(hkb_engine* e, const HostBatch& hb, const DeviceBatch& db,
   fa.h_e_lo = eo->h_e16lo;
   fa.err = e->d_err;
   launch_enc_featurize_tc(st, fa, e->num_sms);
-  e->launches += 2;
+  e->launches += 2;   // kNN, featurisation (memsets are not counted)
   HKB_CUDA(cudaMemsetAsync(eo->h_v, 0, sizeof(float) * R * kH, st));
-  e->launches += 1;
   // TMA tensor maps of h_E (value) for the node and edge passes' tile loads
   if (eo->h_e_rows > SL)
     HKB_CUDA(cudaMemsetAsync(eo->h_e16 + SL * kH, 0,
@@ -954,7 +953,7 @@ hkb_status decoder_tables_tc(hkb_engine* e, const HostBatch& hb, const BatchView
            e->gemm_img.at("dec0.nW1a.lo"), e->w32.dec[0].b1, 0, a0, kH, false, e->d_err);
   tb->Aenc0 = a0;
   tb->h_enc = eo.h_v;
-  e->launches += 5;
+  e->launches += with_pe ? 5 : 4;   // 3 PVenc GEMMs, [slot tables,] Aenc0
   HKB_CUDA(cudaGetLastError());
   return kOk;
 }
